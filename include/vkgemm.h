@@ -1,0 +1,142 @@
+/*
+ * vkgemm -- B200 (sm_100a) GEMM library behind a plain C ABI.
+ *
+ * This is the drop-in boundary for the GEMM hot path of VibeKernel's playground task-1.
+ * The reference's plugin interface is the C++ template
+ *
+ *     template <> void playground::matmul<DType, Version>(size_t m, size_t n, size_t k,
+ *                                                         const DType* A, const DType* B, DType* C);
+ *
+ * declared by PLAYGROUND_MATMUL_DEC and called by PLAYGOUND_MATMUL_CALL
+ * (results/naive_cycle4/include/playground/matmul.hpp:11-23), with one full specialization per
+ * version file `matmul_<dtype>_v<N>_*.cu` (results/naive_cycle6/src/CMakeLists.txt:27-50).  Every
+ * v>=1 specialization in this repository (task-1/src/matmul_f16, task-1/src/matmul_f32) is a
+ * one-line call into the entry points below.
+ *
+ * Conventions (same as the reference):
+ *   - row-major A[m x k], B[k x n], C[m x n]; lda = k, ldb = n, ldc = n unless given;
+ *   - C = A * B (alpha = 1, beta = 0; matmul_f16_v0_cblas.cpp:22-23);
+ *   - device pointers, the call is asynchronous on the given stream (NULL = legacy default
+ *     stream, which is what the reference driver uses, main.cpp:55-62).
+ * Differences (by design): every entry point returns a vk_status instead of exiting; shapes
+ * are int64; there is no CPU fallback -- an unsupported request is an error.
+ */
+#ifndef VKGEMM_H_
+#define VKGEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes.  0 = success; negative = error (details in vk_last_error_string()). */
+typedef enum vk_status {
+    VK_OK = 0,
+    VK_ERR_INVALID_ARGUMENT = -1, /* null pointer, negative size, ld too small, bad enum      */
+    VK_ERR_UNSUPPORTED = -2,      /* combination not implemented (e.g. f32 with f16 acc)      */
+    VK_ERR_CUDA = -3,             /* a CUDA runtime/driver call failed                        */
+    VK_ERR_DEVICE_TIMEOUT = -4,   /* a bounded device-side wait ran out (see vk_device_error) */
+    VK_ERR_NO_DEVICE = -5,        /* no sm_100 device / library built for another arch       */
+    VK_ERR_NCCL = -6,             /* an NCCL call failed in the sharded layer                 */
+    VK_ERR_ALIGNMENT = -7         /* explicitly requested kernel cannot take these strides    */
+} vk_status;
+
+typedef enum vk_dtype {
+    VK_DTYPE_F16 = 0, /* IEEE binary16 in and out (playground::float16_t = half) */
+    VK_DTYPE_F32 = 1  /* IEEE binary32 in and out                                */
+} vk_dtype;
+
+typedef enum vk_acc {
+    VK_ACC_F32 = 0, /* fp32 accumulation (the rubric tier)                  */
+    VK_ACC_F16 = 1  /* fp16 accumulation (tensor-core f16-accumulate tier)   */
+} vk_acc;
+
+typedef enum vk_algo {
+    VK_ALGO_AUTO = 0,     /* pick the fastest kernel that can take the shape/strides          */
+    VK_ALGO_TC_2SM = 1,   /* tcgen05 cta_group::2 pair kernel, 256-row tiles, persistent       */
+    VK_ALGO_TC_1SM = 2,   /* tcgen05 cta_group::1 kernel, 128-row tiles, persistent            */
+    VK_ALGO_FFMA = 3,     /* fp32 CUDA-core SGEMM (register-blocked FFMA)                      */
+    VK_ALGO_SIMT = 4      /* predicated CUDA-core fp16 kernel: any strides/alignment           */
+} vk_algo;
+
+/* One GEMM: C[m x n] = A[m x k] * B[k x n], row-major with leading dimensions in elements. */
+typedef struct vk_gemm_args {
+    const void* A;
+    const void* B;
+    void* C;
+    float* C_f32;   /* optional (may be NULL): fp32 copy of the result before rounding to fp16,
+                       dense m x n (ld = n); used by the verification launch.  fp16 only. */
+    int64_t m, n, k;
+    int64_t lda, ldb, ldc; /* 0 = dense default (k, n, n) */
+    int32_t dtype;         /* vk_dtype */
+    int32_t acc;           /* vk_acc   */
+    int32_t algo;          /* vk_algo  */
+    int32_t tile_n;        /* 0 = default; TC kernels: 128 or 256 (pair tile N)               */
+    void* stream;          /* cudaStream_t; NULL = legacy default stream                       */
+} vk_gemm_args;
+
+/* Replaces: playground::matmul<DType, Version> specialisations, matmul.hpp:16-23.
+ * The general entry point.  Asynchronous; returns before the kernel finishes. */
+int vk_gemm(const vk_gemm_args* args);
+
+/* Replaces: template<> matmul<float16_t, V>(m, n, k, A, B, C), matmul.hpp:16-19 with
+ * DType = float16_t (system.hpp:25).  `version` selects the kernel exactly as the
+ * `--ver N` file does in the reference build (CMakeLists.txt:31-33):
+ *   1 = tcgen05 pair kernel, fp32 accumulate (default champion)
+ *   2 = tcgen05 pair kernel, fp16 accumulate
+ *   3 = tcgen05 single-CTA kernel, fp32 accumulate
+ *   4 = predicated CUDA-core kernel, fp32 accumulate (any alignment)
+ * Version 0 (the cBLAS CPU ground truth) is not part of this library. Default stream. */
+int vk_matmul_f16(int version, size_t m, size_t n, size_t k, const void* A, const void* B, void* C);
+
+/* Replaces: template<> matmul<float32_t, V>(m, n, k, A, B, C), matmul.hpp:16-19 with
+ * DType = float32_t.  version 1 = FFMA SGEMM.  Default stream. */
+int vk_matmul_f32(int version, size_t m, size_t n, size_t k, const float* A, const float* B, float* C);
+
+/* Multi-GPU row-block sharding (no counterpart in the reference, which is single-GPU,
+ * README.md:161; this is the layer BASELINE.json asks for).  GPU r of `ngpu` computes rows
+ * [r*m/ngpu, (r+1)*m/ngpu) of C from its own A slice and a full copy of B; with
+ * allgather_c != 0 an NCCL all-gather then leaves the full C on every GPU.  All pointers
+ * are per-device arrays of length ngpu (A[r] holds only GPU r's rows, dense, ld = k;
+ * B[r] the full k x n matrix; C[r] the full m x n output buffer on GPU r, of which GPU r
+ * writes its own row block).  Synchronous: returns after every GPU finished. */
+typedef struct vk_shard_args {
+    int32_t ngpu;
+    const int32_t* devices;   /* CUDA device ordinals, length ngpu */
+    const void* const* A;     /* per GPU: its (m/ngpu) x k slice  */
+    const void* const* B;     /* per GPU: full k x n              */
+    void* const* C;           /* per GPU: full m x n buffer       */
+    int64_t m, n, k;
+    int32_t dtype, acc, algo; /* as in vk_gemm_args               */
+    int32_t allgather_c;      /* 0 = local row block only          */
+    float* times_ms;          /* optional, length 2: [0] compute max over GPUs, [1] all-gather */
+} vk_shard_args;
+
+int vk_gemm_sharded(const vk_shard_args* args);
+
+/* Device and library state. */
+int vk_init(int device);                 /* optional: warm per-device state (SM count, attrs) */
+int vk_shutdown(void);                   /* frees per-device state and NCCL communicators    */
+const char* vk_last_error_string(void);  /* thread-local message for the last failure        */
+const char* vk_version_string(void);
+
+/* Reads (and optionally clears) the device error word written by a bounded device-side wait
+ * that gave up: 0 = no error, else (code << 32 | detail).  Synchronises the device. */
+int vk_device_error(int device, uint64_t* out_word, int clear);
+
+/* Failure-detection self-test: launches one block whose thread waits on an mbarrier that
+ * nothing arrives on, with the same bounded wait the GEMM kernels use, for `timeout_us`
+ * microseconds.  Returns VK_ERR_DEVICE_TIMEOUT when the wait ran out as designed (and
+ * clears the device error word again), VK_OK never. */
+int vk_selftest_wait_timeout(int device, int64_t timeout_us);
+
+/* Per-call device-side wait limit for the GEMM kernels, nanoseconds (default 2e9). */
+int vk_set_wait_timeout_ns(uint64_t ns);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VKGEMM_H_ */

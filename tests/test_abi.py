@@ -1,0 +1,81 @@
+"""CPU: the C-ABI library loads, exports every entry point the header declares, and rejects
+bad arguments before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "vkgemm.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(vk_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_boundary():
+    names = _declared()
+    for n in ("vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_last_error_string"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    import vibekernel_b200 as vk
+    lib = ctypes.CDLL(vk.LIB_PATH)
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in include/vkgemm.h but not exported"
+    assert set(_declared()) <= set(vk.EXPORTED)
+
+
+def test_library_is_built_for_sm100a_only():
+    import subprocess
+    import vibekernel_b200 as vk
+    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", vk.LIB_PATH],
+                         capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    arches = set(re.findall(r"sm_(\d+a?)", out.stdout))
+    assert arches == {"100a"}, arches
+
+
+def test_argument_validation_without_gpu():
+    import vibekernel_b200 as vk
+    lib = vk.lib
+    assert lib.vk_gemm(None) == vk.VK_ERR_INVALID_ARGUMENT
+    a = vk.GemmArgs()
+    a.m, a.n, a.k = -1, 4, 4
+    assert lib.vk_gemm(ctypes.byref(a)) == vk.VK_ERR_INVALID_ARGUMENT
+    assert "negative" in vk.last_error()
+    a.m = 4
+    a.dtype = 7
+    assert lib.vk_gemm(ctypes.byref(a)) == vk.VK_ERR_INVALID_ARGUMENT
+    a.dtype = vk.DTYPE_F32
+    a.acc = vk.ACC_F16
+    assert lib.vk_gemm(ctypes.byref(a)) == vk.VK_ERR_UNSUPPORTED
+    a.acc = vk.ACC_F32
+    a.algo = 99
+    assert lib.vk_gemm(ctypes.byref(a)) == vk.VK_ERR_INVALID_ARGUMENT
+    a.algo = 0
+    a.lda = 2  # < k
+    assert lib.vk_gemm(ctypes.byref(a)) == vk.VK_ERR_INVALID_ARGUMENT
+    a.lda = 0
+    a.tile_n = 96
+    assert lib.vk_gemm(ctypes.byref(a)) == vk.VK_ERR_INVALID_ARGUMENT
+    assert lib.vk_matmul_f16(0, 4, 4, 4, None, None, None) == vk.VK_ERR_INVALID_ARGUMENT
+    assert lib.vk_matmul_f32(2, 4, 4, 4, None, None, None) == vk.VK_ERR_INVALID_ARGUMENT
+    assert lib.vk_gemm_sharded(None) == vk.VK_ERR_INVALID_ARGUMENT
+    assert lib.vk_set_wait_timeout_ns(0) == vk.VK_ERR_INVALID_ARGUMENT
+    assert vk.version().startswith("vkgemm")
+
+
+def test_no_device_is_an_error_not_a_fallback():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    import vibekernel_b200 as vk
+    a = vk.GemmArgs()
+    a.m = a.n = a.k = 8
+    rc = vk.lib.vk_gemm(ctypes.byref(a))
+    assert rc in (vk.VK_ERR_CUDA, vk.VK_ERR_NO_DEVICE)

@@ -1,0 +1,54 @@
+"""CPU: the row-block sharding logic on 2 gloo ranks (the oracle stands in for the GPU kernel)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import v0
+from vibekernel_b200 import dist_gemm, row_blocks
+
+
+def test_row_blocks_cover_and_balance():
+    for m in (0, 1, 7, 4096, 16384, 4001):
+        for p in (1, 2, 3, 4, 8):
+            off = row_blocks(m, p)
+            assert off[0] == 0 and off[-1] == m
+            sizes = [off[i + 1] - off[i] for i in range(p)]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def _oracle_gemm(A, B, out):
+    out.copy_(torch.from_numpy(v0.v0_f16(A.numpy(), B.numpy())[0]))
+
+
+def _worker(rank, world, port, m, n, k, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        A, B = v0.make_inputs(m, n, k, 3)
+        off = row_blocks(m, world)
+        C = torch.zeros((m, n), dtype=torch.float16)
+        dist_gemm.sharded_matmul(torch.from_numpy(A[off[rank]:off[rank + 1]]), torch.from_numpy(B), C, off,
+                                 rank, _oracle_gemm)
+        ref = v0.v0_f16(A, B)[0]
+        q.put((rank, bool(np.array_equal(C.numpy().view(np.uint16), ref.view(np.uint16)))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("m", [64, 67])  # even split (all-gather) and uneven split (broadcasts)
+def test_two_rank_gloo_sharded_matmul(m):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + m
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, m, 48, 40, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}

@@ -1,0 +1,239 @@
+"""vibekernel_b200 -- Python side of the B200 GEMM library (libvkgemm.so, C ABI in include/vkgemm.h).
+
+Mirrors the reference's plugin interface for the GEMM hot path,
+``template<> void playground::matmul<DType, Version>(m, n, k, A, B, C)``
+(``results/naive_cycle4/include/playground/matmul.hpp:11-23``), as :func:`matmul`, plus the
+general entry point :func:`gemm` (strides, accumulate tier, kernel choice, fp32 copy, stream).
+
+Device memory and streams come from PyTorch (plumbing only); all arithmetic runs in the
+hand-written sm_100a kernels of ``libvkgemm.so``.  There is no CPU fallback: if the library is
+missing, importing this package raises; if no B200 is present, every GPU call raises
+:class:`VkError`.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvkgemm.so")
+
+VK_OK = 0
+VK_ERR_INVALID_ARGUMENT = -1
+VK_ERR_UNSUPPORTED = -2
+VK_ERR_CUDA = -3
+VK_ERR_DEVICE_TIMEOUT = -4
+VK_ERR_NO_DEVICE = -5
+VK_ERR_NCCL = -6
+VK_ERR_ALIGNMENT = -7
+
+DTYPE_F16, DTYPE_F32 = 0, 1
+ACC_F32, ACC_F16 = 0, 1
+ALGO_AUTO, ALGO_TC_2SM, ALGO_TC_1SM, ALGO_FFMA, ALGO_SIMT = 0, 1, 2, 3, 4
+
+_ALGOS = {"auto": ALGO_AUTO, "tc2": ALGO_TC_2SM, "tc1": ALGO_TC_1SM, "ffma": ALGO_FFMA, "simt": ALGO_SIMT}
+_ACCS = {"f32": ACC_F32, "f16": ACC_F16}
+
+# The C-ABI symbols declared in include/vkgemm.h.
+EXPORTED = (
+    "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
+    "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
+    "vk_set_wait_timeout_ns",
+)
+
+
+class VkError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"vkgemm error {code}: {msg}")
+        self.code = code
+
+
+class GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("A", ctypes.c_void_p), ("B", ctypes.c_void_p), ("C", ctypes.c_void_p), ("C_f32", ctypes.c_void_p),
+        ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
+        ("lda", ctypes.c_int64), ("ldb", ctypes.c_int64), ("ldc", ctypes.c_int64),
+        ("dtype", ctypes.c_int32), ("acc", ctypes.c_int32), ("algo", ctypes.c_int32), ("tile_n", ctypes.c_int32),
+        ("stream", ctypes.c_void_p),
+    ]
+
+
+class ShardArgs(ctypes.Structure):
+    _fields_ = [
+        ("ngpu", ctypes.c_int32), ("devices", ctypes.POINTER(ctypes.c_int32)),
+        ("A", ctypes.POINTER(ctypes.c_void_p)), ("B", ctypes.POINTER(ctypes.c_void_p)),
+        ("C", ctypes.POINTER(ctypes.c_void_p)),
+        ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
+        ("dtype", ctypes.c_int32), ("acc", ctypes.c_int32), ("algo", ctypes.c_int32),
+        ("allgather_c", ctypes.c_int32), ("times_ms", ctypes.POINTER(ctypes.c_float)),
+    ]
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is not built; run `python -m vibekernel_b200.build` (nvcc, sm_100a). "
+            "There is no CPU fallback.")
+    lib = ctypes.CDLL(LIB_PATH)
+    lib.vk_gemm.argtypes = [ctypes.POINTER(GemmArgs)]
+    lib.vk_gemm.restype = ctypes.c_int
+    sz = ctypes.c_size_t
+    lib.vk_matmul_f16.argtypes = [ctypes.c_int, sz, sz, sz, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.vk_matmul_f16.restype = ctypes.c_int
+    lib.vk_matmul_f32.argtypes = [ctypes.c_int, sz, sz, sz, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.vk_matmul_f32.restype = ctypes.c_int
+    lib.vk_gemm_sharded.argtypes = [ctypes.POINTER(ShardArgs)]
+    lib.vk_gemm_sharded.restype = ctypes.c_int
+    lib.vk_init.argtypes = [ctypes.c_int]
+    lib.vk_init.restype = ctypes.c_int
+    lib.vk_shutdown.argtypes = []
+    lib.vk_shutdown.restype = ctypes.c_int
+    lib.vk_last_error_string.argtypes = []
+    lib.vk_last_error_string.restype = ctypes.c_char_p
+    lib.vk_version_string.argtypes = []
+    lib.vk_version_string.restype = ctypes.c_char_p
+    lib.vk_device_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]
+    lib.vk_device_error.restype = ctypes.c_int
+    lib.vk_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_int64]
+    lib.vk_selftest_wait_timeout.restype = ctypes.c_int
+    lib.vk_set_wait_timeout_ns.argtypes = [ctypes.c_uint64]
+    lib.vk_set_wait_timeout_ns.restype = ctypes.c_int
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    s = lib.vk_last_error_string()
+    return s.decode() if s else ""
+
+
+def check(rc: int) -> None:
+    if rc != VK_OK:
+        raise VkError(rc, last_error())
+
+
+def version() -> str:
+    return lib.vk_version_string().decode()
+
+
+# ------------------------------------------------------------------------------------------
+# Torch-facing helpers (torch is imported lazily: the C-ABI itself needs no torch)
+# ------------------------------------------------------------------------------------------
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream or None
+    return int(getattr(stream, "cuda_stream", stream)) or None
+
+
+def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile_n: int = 0,
+         stream=None, lda: int = 0, ldb: int = 0, ldc: int = 0, m: int | None = None,
+         n: int | None = None, k: int | None = None):
+    """C = A @ B on the GPU through ``vk_gemm``.
+
+    A [m, k] and B [k, n] are CUDA tensors (fp16, or fp32 for the FFMA kernel), row-major with
+    unit column stride; a row stride larger than the row length is passed as lda/ldb.  Returns C
+    (allocated if not given).  ``c_f32``: optional fp32 [m, n] tensor receiving the result before
+    rounding (fp16 only).  Asynchronous on ``stream`` (default: torch's current stream).
+    """
+    import torch
+    if A.dtype not in (torch.float16, torch.float32) or B.dtype != A.dtype:
+        raise TypeError("A and B must both be float16 or both float32")
+    if not (A.is_cuda and B.is_cuda):
+        raise ValueError("A and B must be CUDA tensors (no CPU fallback)")
+    m = A.shape[0] if m is None else m
+    k = A.shape[1] if k is None else k
+    n = B.shape[1] if n is None else n
+    if A.dim() != 2 or B.dim() != 2 or A.stride(1) != 1 or B.stride(1) != 1:
+        raise ValueError("A and B must be 2-D with unit column stride")
+    lda = lda or A.stride(0)
+    ldb = ldb or B.stride(0)
+    if C is None:
+        C = torch.empty((m, n), dtype=A.dtype, device=A.device)
+    if C.dim() != 2 or C.stride(1) != 1 or C.dtype != A.dtype:
+        raise ValueError("C must be 2-D, unit column stride, same dtype as A")
+    ldc = ldc or C.stride(0)
+    if c_f32 is not None and (c_f32.dtype != torch.float32 or not c_f32.is_contiguous()):
+        raise ValueError("c_f32 must be a contiguous float32 tensor")
+    a = GemmArgs()
+    a.A, a.B, a.C = A.data_ptr(), B.data_ptr(), C.data_ptr()
+    a.C_f32 = c_f32.data_ptr() if c_f32 is not None else None
+    a.m, a.n, a.k = m, n, k
+    a.lda, a.ldb, a.ldc = max(lda, 1), max(ldb, 1), max(ldc, 1)
+    a.dtype = DTYPE_F16 if A.dtype == torch.float16 else DTYPE_F32
+    a.acc = _ACCS[acc]
+    a.algo = _ALGOS[algo]
+    a.tile_n = tile_n
+    a.stream = _stream_handle(stream)
+    with torch.cuda.device(A.device):
+        check(lib.vk_gemm(ctypes.byref(a)))
+    return C
+
+
+def matmul(m: int, n: int, k: int, A, B, C, version: int = 1) -> None:
+    """Mirror of ``playground::matmul<DType, Version>(m, n, k, A, B, C)`` (default stream).
+
+    DType follows the tensors (float16 -> ``vk_matmul_f16``, float32 -> ``vk_matmul_f32``).
+    GPU versions: f16 1 = tcgen05 pair kernel (fp32 acc), 2 = fp16 acc, 3 = single-CTA tcgen05,
+    4 = predicated CUDA-core kernel; f32 1 = FFMA SGEMM.  Version 0 is the reference's CPU
+    ground truth and is not part of this library.
+    """
+    import torch
+    with torch.cuda.device(A.device):
+        if A.dtype == torch.float16:
+            rc = lib.vk_matmul_f16(version, m, n, k, A.data_ptr(), B.data_ptr(), C.data_ptr())
+        elif A.dtype == torch.float32:
+            rc = lib.vk_matmul_f32(version, m, n, k, A.data_ptr(), B.data_ptr(), C.data_ptr())
+        else:
+            raise TypeError("float16 or float32 only")
+    check(rc)
+
+
+def device_error(device: int = 0, clear: bool = True) -> int:
+    w = ctypes.c_uint64(0)
+    check(lib.vk_device_error(device, ctypes.byref(w), 1 if clear else 0))
+    return int(w.value)
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    check(lib.vk_set_wait_timeout_ns(ns))
+
+
+def selftest_wait_timeout(device: int = 0, timeout_us: int = 50000) -> int:
+    """Runs the bounded-wait self-test; returns the status code (VK_ERR_DEVICE_TIMEOUT expected)."""
+    return lib.vk_selftest_wait_timeout(device, timeout_us)
+
+
+def gemm_sharded(A_parts, B_parts, C_parts, m: int, n: int, k: int, *, acc: str = "f32",
+                 algo: str = "auto", allgather: bool = True):
+    """Single-process multi-GPU row-block GEMM through ``vk_gemm_sharded``.
+
+    A_parts[r]: GPU r's row slice [rows_r, k]; B_parts[r]: full [k, n] on GPU r; C_parts[r]: full
+    [m, n] buffer on GPU r.  Returns (compute_ms, gather_ms), each the max over GPUs.
+    """
+    import torch
+    g = len(A_parts)
+    devs = (ctypes.c_int32 * g)(*[t.device.index for t in A_parts])
+    pa = (ctypes.c_void_p * g)(*[t.data_ptr() for t in A_parts])
+    pb = (ctypes.c_void_p * g)(*[t.data_ptr() for t in B_parts])
+    pc = (ctypes.c_void_p * g)(*[t.data_ptr() for t in C_parts])
+    times = (ctypes.c_float * 2)()
+    s = ShardArgs()
+    s.ngpu = g
+    s.devices = devs
+    s.A, s.B, s.C = pa, pb, pc
+    s.m, s.n, s.k = m, n, k
+    s.dtype = DTYPE_F16 if A_parts[0].dtype == torch.float16 else DTYPE_F32
+    s.acc = _ACCS[acc]
+    s.algo = _ALGOS[algo]
+    s.allgather_c = 1 if allgather else 0
+    s.times_ms = times
+    check(lib.vk_gemm_sharded(ctypes.byref(s)))
+    return float(times[0]), float(times[1])
+
+
+def row_blocks(m: int, parts: int):
+    """Row offsets of the balanced split used by the sharded layer: GPU r owns [off[r], off[r+1])."""
+    return [m * r // parts for r in range(parts + 1)]

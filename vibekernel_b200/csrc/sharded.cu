@@ -1,0 +1,243 @@
+// Multi-GPU row-block sharding layer (vk_gemm_sharded) for single-process, multi-device callers
+// such as the task-1 C++ driver.  The reference is single-GPU (README.md:161) and has no NCCL
+// call anywhere; this layer is new.  GPU r computes C[off_r : off_r + rows_r, :] from its own A
+// slice and a full copy of B with the same tensor-core kernel as one GPU (no TMA multicast), on
+// its own stream; the optional exchange is one NCCL all-gather of the C row blocks over NVLink
+// (in place, since C is row-major and the blocks are contiguous), or one broadcast per block
+// when the row split is uneven.  Processes-per-GPU callers (torchrun) shard in Python instead and
+// use torch.distributed for the same all-gather.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <mutex>
+#include <vector>
+
+#include "../../include/vkgemm.h"
+#include "vk_internal.h"
+
+namespace {
+
+// NCCL is resolved lazily with dlopen so that loading the library never pins a libnccl.so.2 of
+// its own: inside a PyTorch process the already-loaded (torch-bundled) NCCL is reused, and a
+// single-GPU caller never needs NCCL at all.
+struct NcclApi {
+    bool loaded = false;
+    ncclResult_t (*CommInitAll)(ncclComm_t*, int, const int*) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+NcclApi g_nccl;
+
+template <typename F>
+bool bind(void* h, const char* name, F& fn)
+{
+    fn = reinterpret_cast<F>(dlsym(h, name));
+    return fn != nullptr;
+}
+
+int load_nccl()
+{
+    if (g_nccl.loaded) return VK_OK;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h == nullptr) return vk::set_error(VK_ERR_NCCL, "cannot load libnccl.so.2: %s", dlerror());
+    bool ok = bind(h, "ncclCommInitAll", g_nccl.CommInitAll) && bind(h, "ncclAllGather", g_nccl.AllGather) &&
+              bind(h, "ncclBroadcast", g_nccl.Broadcast) && bind(h, "ncclGroupStart", g_nccl.GroupStart) &&
+              bind(h, "ncclGroupEnd", g_nccl.GroupEnd) && bind(h, "ncclCommDestroy", g_nccl.CommDestroy) &&
+              bind(h, "ncclGetErrorString", g_nccl.GetErrorString);
+    if (!ok) return vk::set_error(VK_ERR_NCCL, "libnccl.so.2 lacks an expected symbol");
+    g_nccl.loaded = true;
+    return VK_OK;
+}
+
+struct ShardGroup {
+    std::vector<int> devices;
+    std::vector<ncclComm_t> comms;   // empty until the first all-gather
+    std::vector<cudaStream_t> streams;
+    std::vector<cudaEvent_t> ev_start, ev_compute, ev_gather;
+};
+
+std::mutex g_shard_mu;
+std::vector<ShardGroup*> g_groups;
+
+int cuda_err(cudaError_t e, const char* what)
+{
+    return vk::set_error(VK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+ShardGroup* find_or_create(const int32_t* devs, int n, int* rc)
+{
+    for (ShardGroup* g : g_groups) {
+        if (static_cast<int>(g->devices.size()) != n) continue;
+        bool same = true;
+        for (int i = 0; i < n; ++i) same = same && g->devices[i] == devs[i];
+        if (same) return g;
+    }
+    ShardGroup* g = new ShardGroup();
+    g->devices.assign(devs, devs + n);
+    g->streams.resize(n);
+    g->ev_start.resize(n);
+    g->ev_compute.resize(n);
+    g->ev_gather.resize(n);
+    for (int i = 0; i < n; ++i) {
+        cudaError_t e = cudaSetDevice(devs[i]);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&g->streams[i], cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreate(&g->ev_start[i]);
+        if (e == cudaSuccess) e = cudaEventCreate(&g->ev_compute[i]);
+        if (e == cudaSuccess) e = cudaEventCreate(&g->ev_gather[i]);
+        if (e != cudaSuccess) {
+            *rc = cuda_err(e, "shard group setup");
+            return nullptr;  // partially built group is leaked deliberately: it is never reused
+        }
+    }
+    g_groups.push_back(g);
+    return g;
+}
+
+int ensure_comms(ShardGroup* g)
+{
+    if (!g->comms.empty()) return VK_OK;
+    int rc = load_nccl();
+    if (rc != VK_OK) return rc;
+    const int n = static_cast<int>(g->devices.size());
+    g->comms.resize(n);
+    ncclResult_t r = g_nccl.CommInitAll(g->comms.data(), n, g->devices.data());
+    if (r != ncclSuccess) {
+        g->comms.clear();
+        return vk::set_error(VK_ERR_NCCL, "ncclCommInitAll: %s", g_nccl.GetErrorString(r));
+    }
+    return VK_OK;
+}
+
+}  // namespace
+
+extern "C" int vk_gemm_sharded(const vk_shard_args* a)
+{
+    if (a == nullptr) return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: args is NULL");
+    if (a->ngpu < 1 || a->ngpu > 64 || a->devices == nullptr || a->A == nullptr || a->B == nullptr ||
+        a->C == nullptr)
+        return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: bad ngpu or NULL arrays");
+    if (a->m < 0 || a->n < 0 || a->k < 0)
+        return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: negative size");
+    if (a->dtype != VK_DTYPE_F16 && a->dtype != VK_DTYPE_F32)
+        return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: unknown dtype");
+    const int n_gpu = a->ngpu;
+    const size_t esize = a->dtype == VK_DTYPE_F16 ? 2 : 4;
+
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+
+    std::lock_guard<std::mutex> lk(g_shard_mu);
+    int rc = VK_OK;
+    ShardGroup* g = find_or_create(a->devices, n_gpu, &rc);
+    if (g == nullptr) {
+        cudaSetDevice(prev);
+        return rc;
+    }
+    const bool gather = a->allgather_c != 0 && n_gpu > 1;
+    if (gather) {
+        rc = ensure_comms(g);
+        if (rc != VK_OK) {
+            cudaSetDevice(prev);
+            return rc;
+        }
+    }
+
+    std::vector<int64_t> off(n_gpu + 1);
+    for (int r = 0; r <= n_gpu; ++r) off[r] = a->m * r / n_gpu;
+    bool even = true;
+    for (int r = 0; r < n_gpu; ++r) even = even && (off[r + 1] - off[r] == off[1] - off[0]);
+
+    for (int r = 0; r < n_gpu && rc == VK_OK; ++r) {
+        e = cudaSetDevice(a->devices[r]);
+        if (e == cudaSuccess) e = cudaEventRecord(g->ev_start[r], g->streams[r]);
+        if (e != cudaSuccess) {
+            rc = cuda_err(e, "shard start");
+            break;
+        }
+        vk_gemm_args ga = {};
+        ga.A = a->A[r];
+        ga.B = a->B[r];
+        ga.C = static_cast<char*>(a->C[r]) + static_cast<size_t>(off[r]) * a->n * esize;
+        ga.m = off[r + 1] - off[r];
+        ga.n = a->n;
+        ga.k = a->k;
+        ga.dtype = a->dtype;
+        ga.acc = a->acc;
+        ga.algo = a->algo;
+        ga.stream = g->streams[r];
+        rc = vk_gemm(&ga);
+        if (rc != VK_OK) break;
+        e = cudaEventRecord(g->ev_compute[r], g->streams[r]);
+        if (e != cudaSuccess) rc = cuda_err(e, "shard compute event");
+    }
+
+    if (rc == VK_OK && gather) {
+        const ncclDataType_t dt = a->dtype == VK_DTYPE_F16 ? ncclHalf : ncclFloat;
+        ncclResult_t nr = g_nccl.GroupStart();
+        for (int r = 0; r < n_gpu && nr == ncclSuccess; ++r) {
+            char* base = static_cast<char*>(a->C[r]);
+            if (even) {
+                const size_t count = static_cast<size_t>(off[1] - off[0]) * a->n;
+                nr = g_nccl.AllGather(base + static_cast<size_t>(off[r]) * a->n * esize, base, count, dt, g->comms[r],
+                                   g->streams[r]);
+            } else {
+                for (int root = 0; root < n_gpu && nr == ncclSuccess; ++root) {
+                    const size_t count = static_cast<size_t>(off[root + 1] - off[root]) * a->n;
+                    char* blk = base + static_cast<size_t>(off[root]) * a->n * esize;
+                    nr = g_nccl.Broadcast(blk, blk, count, dt, root, g->comms[r], g->streams[r]);
+                }
+            }
+        }
+        ncclResult_t nr2 = g_nccl.GroupEnd();
+        if (nr == ncclSuccess) nr = nr2;
+        if (nr != ncclSuccess) rc = vk::set_error(VK_ERR_NCCL, "all-gather of C: %s", g_nccl.GetErrorString(nr));
+    }
+
+    float t_compute = 0.f, t_gather = 0.f;
+    for (int r = 0; r < n_gpu; ++r) {
+        cudaSetDevice(a->devices[r]);
+        cudaEventRecord(g->ev_gather[r], g->streams[r]);
+        e = cudaStreamSynchronize(g->streams[r]);
+        if (e != cudaSuccess && rc == VK_OK) rc = cuda_err(e, "shard synchronize");
+        if (rc == VK_OK) {
+            float tc = 0.f, tg = 0.f;
+            cudaEventElapsedTime(&tc, g->ev_start[r], g->ev_compute[r]);
+            cudaEventElapsedTime(&tg, g->ev_compute[r], g->ev_gather[r]);
+            if (tc > t_compute) t_compute = tc;
+            if (tg > t_gather) t_gather = tg;
+        }
+    }
+    cudaSetDevice(prev);
+    if (rc == VK_OK && a->times_ms != nullptr) {
+        a->times_ms[0] = t_compute;
+        a->times_ms[1] = gather ? t_gather : 0.f;
+    }
+    return rc;
+}
+
+extern "C" int vk_shutdown(void)
+{
+    std::lock_guard<std::mutex> lk(g_shard_mu);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    for (ShardGroup* g : g_groups) {
+        for (ncclComm_t c : g->comms) g_nccl.CommDestroy(c);
+        for (size_t i = 0; i < g->devices.size(); ++i) {
+            cudaSetDevice(g->devices[i]);
+            cudaStreamDestroy(g->streams[i]);
+            cudaEventDestroy(g->ev_start[i]);
+            cudaEventDestroy(g->ev_compute[i]);
+            cudaEventDestroy(g->ev_gather[i]);
+        }
+        delete g;
+    }
+    g_groups.clear();
+    cudaSetDevice(prev);
+    return VK_OK;
+}

@@ -1,0 +1,222 @@
+// CUDA-core kernels:
+//   * sgemm_ffma_kernel  -- fp32 SGEMM (the reference has only a cBLAS v0 and a library call for
+//     fp32: results/naive/src/matmul_f32/matmul_f32_v0_cblas.cpp:8-12,
+//     results/naive_no_ncu/src/matmul_f32/matmul_f32_v1_cuda-core.cu:10-16).  128 x 128 CTA tile,
+//     8 x 8 outputs per thread in four 4 x 4 quadrants, 128-bit global loads, A staged
+//     transposed, shared-memory double buffering with register prefetch of the next k-slab.
+//   * hgemm_simt_kernel  -- fp16 in, fp32 accumulate, any strides and alignment (the fallback for
+//     shapes the TMA path cannot describe: row pitch not a multiple of 16 bytes).
+//   * fill_zero_kernel   -- C = 0 for k == 0.
+#pragma once
+
+#include <cuda_fp16.h>
+
+namespace vk {
+
+struct SgemmParams {
+    int M, N, K;
+    const float* A;
+    long long lda;
+    const float* B;
+    long long ldb;
+    float* C;
+    long long ldc;
+    int vec_a, vec_b, vec_c;  // 16-byte vector access allowed (alignment of base and ld)
+};
+
+constexpr int kSgBM = 128, kSgBN = 128, kSgBK = 8, kSgThreads = 256;
+constexpr int kSgAPad = 4;  // As row padding (floats): transposed stores hit distinct banks
+
+__device__ __forceinline__ void sg_load_a(const SgemmParams& p, int m0, int k0, float (&ra)[4])
+{
+    const int t = threadIdx.x;
+    const int row = m0 + (t >> 1);
+    const int kc = k0 + (t & 1) * 4;
+    if (row < p.M && p.vec_a && kc + 3 < p.K) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p.A + row * p.lda + kc));
+        ra[0] = v.x;
+        ra[1] = v.y;
+        ra[2] = v.z;
+        ra[3] = v.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            ra[i] = (row < p.M && kc + i < p.K) ? __ldg(p.A + row * p.lda + kc + i) : 0.f;
+    }
+}
+
+__device__ __forceinline__ void sg_load_b(const SgemmParams& p, int n0, int k0, float (&rb)[4])
+{
+    const int t = threadIdx.x;
+    const int kr = k0 + (t >> 5);
+    const int col = n0 + (t & 31) * 4;
+    if (kr < p.K && p.vec_b && col + 3 < p.N) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p.B + kr * p.ldb + col));
+        rb[0] = v.x;
+        rb[1] = v.y;
+        rb[2] = v.z;
+        rb[3] = v.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            rb[i] = (kr < p.K && col + i < p.N) ? __ldg(p.B + kr * p.ldb + col + i) : 0.f;
+    }
+}
+
+__global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_kernel(const SgemmParams p)
+{
+    __shared__ __align__(16) float As[2][kSgBK][kSgBM + kSgAPad];
+    __shared__ __align__(16) float Bs[2][kSgBK][kSgBN];
+
+    const int t = threadIdx.x;
+    const int tx = t & 15;
+    const int ty = t >> 4;
+    const int m0 = blockIdx.y * kSgBM;
+    const int n0 = blockIdx.x * kSgBN;
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+    float ra[4], rb[4];
+    sg_load_a(p, m0, 0, ra);
+    sg_load_b(p, n0, 0, rb);
+    {
+        const int ar = t >> 1, ak = (t & 1) * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) As[0][ak + i][ar] = ra[i];
+        *reinterpret_cast<float4*>(&Bs[0][t >> 5][(t & 31) * 4]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+    }
+    __syncthreads();
+
+    const int nk = (p.K + kSgBK - 1) / kSgBK;
+    for (int kt = 0; kt < nk; ++kt) {
+        const int cur = kt & 1;
+        const bool has_next = kt + 1 < nk;
+        if (has_next) {
+            sg_load_a(p, m0, (kt + 1) * kSgBK, ra);
+            sg_load_b(p, n0, (kt + 1) * kSgBK, rb);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kSgBK; ++kk) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][kk][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][kk][ty * 4 + 64]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][kk][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][kk][tx * 4 + 64]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (has_next) {
+            const int nxt = cur ^ 1;
+            const int ar = t >> 1, ak = (t & 1) * 4;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) As[nxt][ak + i][ar] = ra[i];
+            *reinterpret_cast<float4*>(&Bs[nxt][t >> 5][(t & 31) * 4]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+        }
+        __syncthreads();
+    }
+
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int row = m0 + ty * 4 + (i & 3) + (i >> 2) * 64;
+        if (row >= p.M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int col = n0 + tx * 4 + h * 64;
+            float* dst = p.C + row * p.ldc + col;
+            if (p.vec_c && col + 3 < p.N) {
+                *reinterpret_cast<float4*>(dst) =
+                    make_float4(acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (col + j < p.N) dst[j] = acc[i][4 * h + j];
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+struct HgemmSimtParams {
+    int M, N, K;
+    const __half* A;
+    long long lda;
+    const __half* B;
+    long long ldb;
+    __half* C;
+    long long ldc;
+    float* C32;  // optional fp32 copy, ld = N
+};
+
+constexpr int kHsTile = 64, kHsBK = 16;
+
+// 64 x 64 tile, 256 threads, 4 x 4 outputs per thread, scalar predicated loads.
+__global__ void __launch_bounds__(256) hgemm_simt_kernel(const HgemmSimtParams p)
+{
+    __shared__ float As[kHsBK][kHsTile + 1];
+    __shared__ float Bs[kHsBK][kHsTile + 1];
+    const int t = threadIdx.x;
+    const int tx = t & 15, ty = t >> 4;
+    const int m0 = blockIdx.y * kHsTile, n0 = blockIdx.x * kHsTile;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < p.K; k0 += kHsBK) {
+        for (int e = t; e < kHsTile * kHsBK; e += 256) {
+            const int r = e / kHsBK, c = e % kHsBK;  // A: row r, k c
+            const int gr = m0 + r, gk = k0 + c;
+            As[c][r] = (gr < p.M && gk < p.K) ? __half2float(p.A[gr * p.lda + gk]) : 0.f;
+            const int kr = e / kHsTile, nc = e % kHsTile;  // B: k kr, col nc
+            const int bk = k0 + kr, bn = n0 + nc;
+            Bs[kr][nc] = (bk < p.K && bn < p.N) ? __half2float(p.B[bk * p.ldb + bn]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < kHsBK; ++kk) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int row = m0 + ty + 16 * i;
+        if (row >= p.M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int col = n0 + tx + 16 * j;
+            if (col >= p.N) continue;
+            p.C[row * p.ldc + col] = __float2half_rn(acc[i][j]);
+            if (p.C32 != nullptr) p.C32[static_cast<long long>(row) * p.N + col] = acc[i][j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void fill_zero_kernel(T* C, long long ldc, int M, int N, float* C32)
+{
+    const long long total = static_cast<long long>(M) * N;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / N, c = i % N;
+        C[r * ldc + c] = T(0.f);
+        if (C32 != nullptr) C32[i] = 0.f;
+    }
+}
+
+// Failure-detection self-test: one thread waits on an mbarrier nothing arrives on.
+__global__ void selftest_wait_kernel(unsigned long long timeout_ns);
+
+}  // namespace vk

@@ -1,0 +1,336 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a:  C[M,N] = A[M,K] * B[K,N], fp16 in,
+// fp32 (or fp16) accumulate in tensor memory, fp16 out (+ optional fp32 copy).
+//
+// Replaces the A100 mma.sync/cp.async kernels behind playground::matmul<float16_t, V>
+// (e.g. results/ralph_loop_fable/src/matmul_f16/matmul_f16_v42_shfl2.cu:104-490): same row-major
+// NN contract, but the math is tcgen05.mma issued by one thread with accumulators in TMEM, the
+// operands arrive by TMA into 128-byte-swizzled shared memory, and a pair of CTAs (cta_group::2)
+// shares one 256-row tile.
+//
+// Roles (192 threads per CTA):
+//   warp 0      TMA producer: one lane streams A (K-major) and B (N-major) k-blocks into a ring
+//               of STAGES shared-memory stages guarded by full/empty mbarriers.
+//   warp 1      TMEM allocator (whole warp) and, in the pair's leader CTA, the MMA issuer (one
+//               lane).  Two accumulators (2 x BN TMEM columns) alternate between tiles, so the
+//               epilogue of tile i overlaps the main loop of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, convert, store to global.
+//
+// Pair mode (CG = 2): the two CTAs of a cluster each hold 128 rows of A and BN/2 columns of B
+// per stage; the leader issues 256 x BN x 16 MMAs that read both CTAs' shared memory and write
+// both CTAs' TMEM.  Both CTAs' TMA loads signal the leader's "full" barrier (.cta_group::2
+// completion), and the leader's commits arrive on both CTAs' "empty" and "tmem full" barriers.
+// No TMA multicast is used anywhere, so the same binary serves 1-GPU and multi-GPU runs.
+//
+// Ragged shapes: TMA zero-fills out-of-range rows/columns of A and B (M, N and the K tail);
+// the epilogue predicates stores on row < M and col < N.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace vk {
+
+struct TcParams {
+    int M, N, K;
+    int tiles_m, tiles_n, num_kb;
+    int raster_group;        // tiles along M per rasterisation group
+    __half* C;
+    long long ldc;
+    float* C32;              // optional fp32 copy, ld = N
+    int vec_ok;              // C / C32 alignment allows 16-byte stores
+    unsigned long long timeout_ns;
+};
+
+template <int CG, int BN, int STAGES, bool ACC_F32>
+struct TcCfg {
+    static constexpr int kBM = 128;              // rows per CTA (TMEM lanes)
+    static constexpr int kBK = 64;               // k per stage = one 128-byte swizzle span of fp16
+    static constexpr int kBNCta = BN / CG;       // B columns held per CTA
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = kBNCta * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBBoxes = kBNCta / 64;  // 64-column TMA boxes of B per stage
+    static constexpr int kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
+                                   : (2 * BN <= 256) ? 256 : 512;
+    static constexpr int kNumBars = 2 * STAGES + 4;
+    static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kNumBars * 8 + 16;
+    static constexpr int kThreads = 192;
+    static_assert(CG == 1 || CG == 2, "cta group");
+    static_assert(kBNCta % 64 == 0, "each CTA holds whole 64-column swizzle atoms of B");
+    static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "UMMA N");
+    static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
+    static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group, int& tm, int& tn)
+{
+    const int per_group = group * tiles_n;
+    const int g = t / per_group;
+    const int first_m = g * group;
+    const int gsz = min(tiles_m - first_m, group);
+    const int r = t - g * per_group;
+    tm = first_m + r % gsz;
+    tn = r / gsz;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
+{
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Store one row's 32 consecutive results (r = raw TMEM words) at C[row, col .. col+31].
+template <bool ACC_F32>
+__device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col, const uint32_t (&r)[32])
+{
+    if (row >= p.M) return;
+    __half* crow = p.C + static_cast<long long>(row) * p.ldc;
+    const bool full = (col + 32 <= p.N) && p.vec_ok;
+    if (full) {
+        uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint4 v;
+            if constexpr (ACC_F32) {
+                v.x = pack_half2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+                v.y = pack_half2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+                v.z = pack_half2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+                v.w = pack_half2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+            } else {
+                // fp16 accumulators occupy the low 16 bits of each 32-bit TMEM column.
+                v.x = __byte_perm(r[8 * j + 0], r[8 * j + 1], 0x5410);
+                v.y = __byte_perm(r[8 * j + 2], r[8 * j + 3], 0x5410);
+                v.z = __byte_perm(r[8 * j + 4], r[8 * j + 5], 0x5410);
+                v.w = __byte_perm(r[8 * j + 6], r[8 * j + 7], 0x5410);
+            }
+            dst[j] = v;
+        }
+        if (p.C32 != nullptr) {
+            float4* d32 = reinterpret_cast<float4*>(p.C32 + static_cast<long long>(row) * p.N + col);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float4 f;
+                if constexpr (ACC_F32) {
+                    f = make_float4(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1]),
+                                    __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+                } else {
+                    f = make_float4(__half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 0]))),
+                                    __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 1]))),
+                                    __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 2]))),
+                                    __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 3]))));
+                }
+                d32[j] = f;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (col + i < p.N) {
+                float f;
+                __half h;
+                if constexpr (ACC_F32) {
+                    f = __uint_as_float(r[i]);
+                    h = __float2half_rn(f);
+                } else {
+                    h = __ushort_as_half(static_cast<unsigned short>(r[i]));
+                    f = __half2float(h);
+                }
+                crow[col + i] = h;
+                if (p.C32 != nullptr) p.C32[static_cast<long long>(row) * p.N + col + i] = f;
+            }
+        }
+    }
+}
+
+template <int CG, int BN, int STAGES, bool ACC_F32>
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                   const TcParams p)
+{
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+    using Cfg = TcCfg<CG, BN, STAGES, ACC_F32>;
+    constexpr int BM = Cfg::kBM;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * Cfg::kABytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kBBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+    const int cluster_id = blockIdx.x / CG;
+    const int num_clusters = gridDim.x / CG;
+    const int num_tiles = p.tiles_m * p.tiles_n;
+
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), CG * 4);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc<CG>(smem_u32(tmem_slot), Cfg::kTmemCols);
+        tmem_relinquish<CG>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if constexpr (CG == 2) cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+                int tm, tn;
+                tile_coords(t, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
+                const int m0 = tm * (BM * CG) + static_cast<int>(rank) * BM;
+                const int n0 = tn * BN + static_cast<int>(rank) * Cfg::kBNCta;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, kErrWaitProducer, stage)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full_bar(stage);
+                    const uint32_t a_dst = smem_u32(sA + stage * Cfg::kABytes);
+                    const uint32_t b_dst = smem_u32(sB + stage * Cfg::kBBytes);
+                    const int k0 = kb * Cfg::kBK;
+                    if constexpr (CG == 1) {
+                        mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+                        tma_load_2d(a_dst, &tmap_a, fb, k0, m0);
+#pragma unroll
+                        for (int j = 0; j < Cfg::kBBoxes; ++j)
+                            tma_load_2d(b_dst + j * 8192, &tmap_b, fb, n0 + 64 * j, k0);
+                    } else {
+                        if (rank == 0) mbar_arrive_expect_tx(fb, 2 * Cfg::kStageBytes);
+                        const uint32_t fb_leader = mapa_shared(fb, 0);
+                        tma_load_2d_pair(a_dst, &tmap_a, fb_leader, k0, m0);
+#pragma unroll
+                        for (int j = 0; j < Cfg::kBBoxes; ++j)
+                            tma_load_2d_pair(b_dst + j * 8192, &tmap_b, fb_leader, n0 + 64 * j, k0);
+                    }
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain: every stage this CTA filled must be released by the MMA (whose commits may
+            // arrive from the peer CTA) before the CTA may exit.
+            if (ok) {
+                for (int i = 0; i < STAGES; ++i) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, kErrWaitTail, stage)) break;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (rank == 0 && lane == 0) {
+            constexpr uint32_t kIdesc = idesc_f16(BM * CG, BN, ACC_F32, /*b_mn_major=*/true);
+            // B is N-major: 64-column atoms of BK rows x 128 B; LBO steps between atoms, SBO
+            // between 8-row groups.  A is K-major: SBO steps between 8-row groups.
+            constexpr uint32_t kBLbo = Cfg::kBK * 128;
+            int stage = 0;
+            uint32_t phase = 0;
+            int it = 0;
+            bool ok = true;
+            for (int t = cluster_id; ok && t < num_tiles; t += num_clusters, ++it) {
+                const int acc = it & 1;
+                const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, kErrWaitMma, 100 + acc)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, kErrWaitMma, stage)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+                    const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
+                        const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+                        const uint64_t b_desc = smem_desc_sw128(b_addr + kk * 16 * 128, kBLbo, 1024);
+                        umma_f16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    const uint32_t eb = empty_bar(stage);
+                    umma_commit<CG>(eb);
+                    if constexpr (CG == 2) umma_commit<CG>(mapa_shared(eb, 1));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                const uint32_t tb = tfull_bar(acc);
+                umma_commit<CG>(tb);
+                if constexpr (CG == 2) umma_commit<CG>(mapa_shared(tb, 1));
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int it = 0;
+        for (int t = cluster_id; t < num_tiles; t += num_clusters, ++it) {
+            const int acc = it & 1;
+            const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
+            if (!mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, kErrWaitEpilogue, acc)) break;
+            tc_fence_after();
+            int tm, tn;
+            tile_coords(t, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
+            const int row = tm * (BM * CG) + static_cast<int>(rank) * BM + q * 32 + lane;
+            const int col0 = tn * BN;
+            const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
+                tmem_ld_wait();
+                if (col0 + c < p.N) store_chunk<ACC_F32>(p, row, col0 + c, r);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (CG == 1)
+                    mbar_arrive(tempty_bar(acc));
+                else
+                    mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if constexpr (CG == 2) cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc<CG>(tmem_base, Cfg::kTmemCols);
+    }
+#endif
+}
+
+}  // namespace vk

@@ -1,0 +1,7 @@
+// Internal helpers shared by the translation units of libvkgemm.so (not part of the C ABI).
+#pragma once
+
+namespace vk {
+// Records a thread-local error message (read back by vk_last_error_string) and returns `code`.
+int set_error(int code, const char* fmt, ...);
+}  // namespace vk

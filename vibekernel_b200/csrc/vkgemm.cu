@@ -1,0 +1,519 @@
+// C-ABI implementation of include/vkgemm.h: argument checking, kernel selection, TMA tensor-map
+// encoding, persistent-grid sizing and launches.  Single translation unit for all device code
+// (no relocatable device code needed).
+//
+// Host-side state mirrors what the reference kernels keep in function-static variables
+// (results/ralph_loop_fable/src/matmul_f16/matmul_f16_v42_shfl2.cu:496-518: SM count, smem
+// attribute, workspace) but is per device, mutex-protected, and released by vk_shutdown().
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/vkgemm.h"
+#include "ptx.cuh"
+#include "simt_gemm.cuh"
+#include "tc_gemm.cuh"
+#include "vk_internal.h"
+
+namespace vk {
+
+__global__ void selftest_wait_kernel(unsigned long long timeout_ns)
+{
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        fence_mbar_init();
+        // Nothing ever arrives: the bounded wait must give up and record kErrWaitSelftest.
+        (void)mbar_wait(smem_u32(&bar), 0u, timeout_ns, kErrWaitSelftest, 0);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Errors
+// ------------------------------------------------------------------------------------------
+static thread_local std::string t_last_error;
+
+int set_error(int code, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* what)
+{
+    return set_error(VK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define VK_CUDA_TRY(expr)                                  \
+    do {                                                   \
+        cudaError_t _e = (expr);                           \
+        if (_e != cudaSuccess) return cuda_fail(_e, #expr); \
+    } while (0)
+
+// ------------------------------------------------------------------------------------------
+// Per-device state
+// ------------------------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+constexpr int kMaxKernels = 32;
+
+struct KernelSlot {
+    const void* fn = nullptr;
+    int max_clusters = 0;  // co-resident clusters (CG=2) or CTAs (CG=1) at this smem size
+};
+
+struct DeviceState {
+    std::atomic<bool> ready{false};
+    int sm_count = 0;
+    KernelSlot kernels[kMaxKernels];
+    int num_kernels = 0;
+};
+
+static std::mutex g_mu;
+static DeviceState g_dev[kMaxDevices];
+static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn g_encode = nullptr;
+
+static int init_device_locked(int dev)
+{
+    DeviceState& st = g_dev[dev];
+    if (st.ready.load(std::memory_order_acquire)) return VK_OK;
+    cudaDeviceProp prop;
+    VK_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10 || prop.minor != 0)
+        return set_error(VK_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
+                         prop.major, prop.minor);
+    st.sm_count = prop.multiProcessorCount;
+    if (g_encode == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        VK_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || fn == nullptr)
+            return set_error(VK_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+        g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    st.ready.store(true, std::memory_order_release);
+    return VK_OK;
+}
+
+int current_device(int* dev_out, DeviceState** st_out)
+{
+    int dev = 0;
+    VK_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return set_error(VK_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+    DeviceState& st = g_dev[dev];
+    if (!st.ready.load(std::memory_order_acquire)) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        int rc = init_device_locked(dev);
+        if (rc != VK_OK) return rc;
+    }
+    *dev_out = dev;
+    if (st_out) *st_out = &st;
+    return VK_OK;
+}
+
+// Sets the smem attribute once per (device, kernel) and caches the co-residency limit.
+template <typename Kernel>
+static int kernel_slot(DeviceState& st, Kernel fn, int smem, int threads, int cluster, int* max_units)
+{
+    const void* key = reinterpret_cast<const void*>(fn);
+    for (int i = 0; i < st.num_kernels; ++i) {
+        if (st.kernels[i].fn == key) {
+            *max_units = st.kernels[i].max_clusters;
+            return VK_OK;
+        }
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (int i = 0; i < st.num_kernels; ++i) {
+        if (st.kernels[i].fn == key) {
+            *max_units = st.kernels[i].max_clusters;
+            return VK_OK;
+        }
+    }
+    if (st.num_kernels >= kMaxKernels) return set_error(VK_ERR_UNSUPPORTED, "kernel table full");
+    VK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    int units = 0;
+    if (cluster > 1) {
+        VK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = cluster;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(cluster * st.sm_count, 1, 1);
+        cfg.blockDim = dim3(threads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        VK_CUDA_TRY(cudaOccupancyMaxActiveClusters(&units, fn, &cfg));
+    } else {
+        int per_sm = 0;
+        VK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));
+        units = per_sm * st.sm_count;
+    }
+    if (units <= 0) return set_error(VK_ERR_CUDA, "kernel cannot be resident (smem %d)", smem);
+    KernelSlot& s = st.kernels[st.num_kernels];
+    s.fn = key;
+    s.max_clusters = units;
+    st.num_kernels++;
+    *max_units = units;
+    return VK_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Tensor maps
+// ------------------------------------------------------------------------------------------
+// 2-D fp16 tensor map over a row-major matrix [rows x cols] with row pitch `ld` elements and a
+// (box_cols x box_rows) box, 128-byte swizzle, zero fill outside the matrix.
+static int make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                         uint32_t box_cols, uint32_t box_rows)
+{
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(VK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld", (int)r,
+                         (long long)rows, (long long)cols, (long long)ld);
+    return VK_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Launchers
+// ------------------------------------------------------------------------------------------
+struct Problem {
+    const void* A;
+    const void* B;
+    void* C;
+    float* C32;
+    int64_t m, n, k, lda, ldb, ldc;
+    cudaStream_t stream;
+    int tile_n;
+};
+
+template <int CG, int BN, int STAGES, bool ACC_F32>
+static int launch_tc(DeviceState& st, const Problem& pb)
+{
+    using Cfg = TcCfg<CG, BN, STAGES, ACC_F32>;
+    auto fn = tc_gemm_kernel<CG, BN, STAGES, ACC_F32>;
+    int max_units = 0;
+    int rc = kernel_slot(st, fn, Cfg::kSmemBytes, Cfg::kThreads, CG, &max_units);
+    if (rc != VK_OK) return rc;
+
+    CUtensorMap ta, tb;
+    rc = make_tmap_f16(&ta, pb.A, pb.m, pb.k, pb.lda, 64, Cfg::kBM);
+    if (rc != VK_OK) return rc;
+    rc = make_tmap_f16(&tb, pb.B, pb.k, pb.n, pb.ldb, 64, Cfg::kBK);
+    if (rc != VK_OK) return rc;
+
+    TcParams p;
+    p.M = static_cast<int>(pb.m);
+    p.N = static_cast<int>(pb.n);
+    p.K = static_cast<int>(pb.k);
+    p.tiles_m = static_cast<int>((pb.m + Cfg::kBM * CG - 1) / (Cfg::kBM * CG));
+    p.tiles_n = static_cast<int>((pb.n + BN - 1) / BN);
+    p.num_kb = static_cast<int>((pb.k + Cfg::kBK - 1) / Cfg::kBK);
+    p.raster_group = 8;
+    p.C = static_cast<__half*>(pb.C);
+    p.ldc = pb.ldc;
+    p.C32 = pb.C32;
+    const bool c_vec = (reinterpret_cast<uintptr_t>(pb.C) % 16 == 0) && (pb.ldc % 8 == 0);
+    const bool c32_vec = pb.C32 == nullptr || ((reinterpret_cast<uintptr_t>(pb.C32) % 16 == 0) && (pb.n % 4 == 0));
+    p.vec_ok = (c_vec && c32_vec) ? 1 : 0;
+    p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
+
+    const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+    const int clusters = static_cast<int>(tiles < max_units ? tiles : max_units);
+
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(CG * clusters, 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = pb.stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VK_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, ta, tb, p));
+    return VK_OK;
+}
+
+static int launch_sgemm(const Problem& pb)
+{
+    SgemmParams p;
+    p.M = static_cast<int>(pb.m);
+    p.N = static_cast<int>(pb.n);
+    p.K = static_cast<int>(pb.k);
+    p.A = static_cast<const float*>(pb.A);
+    p.B = static_cast<const float*>(pb.B);
+    p.C = static_cast<float*>(pb.C);
+    p.lda = pb.lda;
+    p.ldb = pb.ldb;
+    p.ldc = pb.ldc;
+    p.vec_a = (reinterpret_cast<uintptr_t>(pb.A) % 16 == 0) && (pb.lda % 4 == 0);
+    p.vec_b = (reinterpret_cast<uintptr_t>(pb.B) % 16 == 0) && (pb.ldb % 4 == 0);
+    p.vec_c = (reinterpret_cast<uintptr_t>(pb.C) % 16 == 0) && (pb.ldc % 4 == 0);
+    dim3 grid(static_cast<unsigned>((pb.n + kSgBN - 1) / kSgBN), static_cast<unsigned>((pb.m + kSgBM - 1) / kSgBM));
+    if (grid.y > 65535u) return set_error(VK_ERR_UNSUPPORTED, "m too large for the SGEMM grid");
+    sgemm_ffma_kernel<<<grid, kSgThreads, 0, pb.stream>>>(p);
+    VK_CUDA_TRY(cudaGetLastError());
+    return VK_OK;
+}
+
+static int launch_hgemm_simt(const Problem& pb)
+{
+    HgemmSimtParams p;
+    p.M = static_cast<int>(pb.m);
+    p.N = static_cast<int>(pb.n);
+    p.K = static_cast<int>(pb.k);
+    p.A = static_cast<const __half*>(pb.A);
+    p.B = static_cast<const __half*>(pb.B);
+    p.C = static_cast<__half*>(pb.C);
+    p.lda = pb.lda;
+    p.ldb = pb.ldb;
+    p.ldc = pb.ldc;
+    p.C32 = pb.C32;
+    dim3 grid(static_cast<unsigned>((pb.n + kHsTile - 1) / kHsTile), static_cast<unsigned>((pb.m + kHsTile - 1) / kHsTile));
+    if (grid.y > 65535u) return set_error(VK_ERR_UNSUPPORTED, "m too large for the SIMT grid");
+    hgemm_simt_kernel<<<grid, 256, 0, pb.stream>>>(p);
+    VK_CUDA_TRY(cudaGetLastError());
+    return VK_OK;
+}
+
+template <typename T>
+static int launch_zero(DeviceState& st, const Problem& pb)
+{
+    const long long total = pb.m * pb.n;
+    long long blocks = (total + 255) / 256;
+    if (blocks > 8LL * st.sm_count) blocks = 8LL * st.sm_count;
+    fill_zero_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, pb.stream>>>(
+        static_cast<T*>(pb.C), pb.ldc, static_cast<int>(pb.m), static_cast<int>(pb.n), pb.C32);
+    VK_CUDA_TRY(cudaGetLastError());
+    return VK_OK;
+}
+
+static bool tma_ok_f16(const void* p, int64_t ld)
+{
+    return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && ((ld * 2) % 16 == 0) && (ld * 2 < (1LL << 40));
+}
+
+}  // namespace vk
+
+// ==========================================================================================
+// C ABI
+// ==========================================================================================
+using namespace vk;
+
+extern "C" int vk_gemm(const vk_gemm_args* a)
+{
+    if (a == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: args is NULL");
+    if (a->m < 0 || a->n < 0 || a->k < 0)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: negative size m=%lld n=%lld k=%lld", (long long)a->m,
+                         (long long)a->n, (long long)a->k);
+    const int64_t kMaxDim = (1LL << 31) - 1;
+    if (a->m > kMaxDim || a->n > kMaxDim || a->k > kMaxDim)
+        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: dimensions above 2^31-1 are not supported");
+    if (a->dtype != VK_DTYPE_F16 && a->dtype != VK_DTYPE_F32)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: unknown dtype %d", a->dtype);
+    if (a->acc != VK_ACC_F32 && a->acc != VK_ACC_F16)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: unknown acc %d", a->acc);
+    if (a->algo < VK_ALGO_AUTO || a->algo > VK_ALGO_SIMT)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: unknown algo %d", a->algo);
+
+    Problem pb;
+    pb.A = a->A;
+    pb.B = a->B;
+    pb.C = a->C;
+    pb.C32 = a->C_f32;
+    pb.m = a->m;
+    pb.n = a->n;
+    pb.k = a->k;
+    pb.lda = a->lda ? a->lda : a->k;
+    pb.ldb = a->ldb ? a->ldb : a->n;
+    pb.ldc = a->ldc ? a->ldc : a->n;
+    pb.stream = static_cast<cudaStream_t>(a->stream);
+    pb.tile_n = a->tile_n;
+    if (pb.lda < pb.k || pb.ldb < pb.n || pb.ldc < pb.n || pb.lda < 0 || pb.ldb < 0 || pb.ldc < 0)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: leading dimension smaller than the row length");
+    if (a->dtype == VK_DTYPE_F32 && a->acc != VK_ACC_F32)
+        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: fp32 GEMM supports fp32 accumulation only");
+    if (a->dtype == VK_DTYPE_F32 && a->C_f32 != nullptr)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: C_f32 copy is for fp16 output only");
+    if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: tile_n must be 0, 128 or 256");
+
+    int dev = 0;
+    DeviceState* st = nullptr;
+    int rc = current_device(&dev, &st);
+    if (rc != VK_OK) return rc;
+
+    if (pb.m == 0 || pb.n == 0) return VK_OK;
+    if (pb.C == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: C is NULL");
+    if (pb.k == 0) return a->dtype == VK_DTYPE_F16 ? launch_zero<__half>(*st, pb) : launch_zero<float>(*st, pb);
+    if (pb.A == nullptr || pb.B == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: A or B is NULL");
+
+    if (a->dtype == VK_DTYPE_F32) {
+        if (a->algo != VK_ALGO_AUTO && a->algo != VK_ALGO_FFMA)
+            return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: fp32 runs on the FFMA kernel only");
+        return launch_sgemm(pb);
+    }
+
+    // fp16
+    const bool tma_ok = tma_ok_f16(pb.A, pb.lda) && tma_ok_f16(pb.B, pb.ldb);
+    int algo = a->algo;
+    if (algo == VK_ALGO_FFMA) return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: FFMA kernel is fp32 only");
+    if (algo == VK_ALGO_AUTO) algo = tma_ok ? VK_ALGO_TC_2SM : VK_ALGO_SIMT;
+    if (algo == VK_ALGO_SIMT) {
+        if (a->acc != VK_ACC_F32)
+            return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: the predicated CUDA-core kernel accumulates in fp32 only");
+        return launch_hgemm_simt(pb);
+    }
+    if (!tma_ok)
+        return set_error(VK_ERR_ALIGNMENT,
+                         "vk_gemm: tensor-core kernels need 16-byte aligned A/B and lda, ldb multiples of 8 "
+                         "(use VK_ALGO_AUTO or VK_ALGO_SIMT)");
+    const int tn = pb.tile_n ? pb.tile_n : 256;
+    const bool f32 = a->acc == VK_ACC_F32;
+    if (algo == VK_ALGO_TC_2SM) {
+        if (tn == 256) return f32 ? launch_tc<2, 256, 6, true>(*st, pb) : launch_tc<2, 256, 6, false>(*st, pb);
+        return f32 ? launch_tc<2, 128, 8, true>(*st, pb) : launch_tc<2, 128, 8, false>(*st, pb);
+    }
+    if (tn == 256) return f32 ? launch_tc<1, 256, 4, true>(*st, pb) : launch_tc<1, 256, 4, false>(*st, pb);
+    return f32 ? launch_tc<1, 128, 6, true>(*st, pb) : launch_tc<1, 128, 6, false>(*st, pb);
+}
+
+extern "C" int vk_matmul_f16(int version, size_t m, size_t n, size_t k, const void* A, const void* B, void* C)
+{
+    vk_gemm_args a;
+    memset(&a, 0, sizeof(a));
+    a.A = A;
+    a.B = B;
+    a.C = C;
+    a.m = static_cast<int64_t>(m);
+    a.n = static_cast<int64_t>(n);
+    a.k = static_cast<int64_t>(k);
+    a.dtype = VK_DTYPE_F16;
+    switch (version) {
+        case 1: a.algo = VK_ALGO_TC_2SM; a.acc = VK_ACC_F32; break;
+        case 2: a.algo = VK_ALGO_TC_2SM; a.acc = VK_ACC_F16; break;
+        case 3: a.algo = VK_ALGO_TC_1SM; a.acc = VK_ACC_F32; break;
+        case 4: a.algo = VK_ALGO_SIMT; a.acc = VK_ACC_F32; break;
+        default:
+            return set_error(VK_ERR_INVALID_ARGUMENT,
+                             "vk_matmul_f16: version %d is not a GPU version (1..4; v0 is the CPU ground truth)",
+                             version);
+    }
+    return vk_gemm(&a);
+}
+
+extern "C" int vk_matmul_f32(int version, size_t m, size_t n, size_t k, const float* A, const float* B, float* C)
+{
+    if (version != 1)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_matmul_f32: version %d is not a GPU version (1)", version);
+    vk_gemm_args a;
+    memset(&a, 0, sizeof(a));
+    a.A = A;
+    a.B = B;
+    a.C = C;
+    a.m = static_cast<int64_t>(m);
+    a.n = static_cast<int64_t>(n);
+    a.k = static_cast<int64_t>(k);
+    a.dtype = VK_DTYPE_F32;
+    a.acc = VK_ACC_F32;
+    a.algo = VK_ALGO_FFMA;
+    return vk_gemm(&a);
+}
+
+extern "C" int vk_init(int device)
+{
+    int prev = 0;
+    VK_CUDA_TRY(cudaGetDevice(&prev));
+    VK_CUDA_TRY(cudaSetDevice(device));
+    int dev = 0;
+    int rc = current_device(&dev, nullptr);
+    cudaSetDevice(prev);
+    return rc;
+}
+
+extern "C" const char* vk_last_error_string(void) { return t_last_error.c_str(); }
+
+extern "C" const char* vk_version_string(void) { return "vkgemm 0.1.0 (sm_100a)"; }
+
+extern "C" int vk_set_wait_timeout_ns(uint64_t ns)
+{
+    if (ns == 0) return set_error(VK_ERR_INVALID_ARGUMENT, "timeout must be > 0");
+    g_timeout_ns.store(ns);
+    return VK_OK;
+}
+
+extern "C" int vk_device_error(int device, uint64_t* out_word, int clear)
+{
+    if (out_word == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "out_word is NULL");
+    int prev = 0;
+    VK_CUDA_TRY(cudaGetDevice(&prev));
+    VK_CUDA_TRY(cudaSetDevice(device));
+    unsigned long long w = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&w, g_device_error, sizeof(w));
+    if (e == cudaSuccess && clear && w != 0) {
+        const unsigned long long z = 0;
+        e = cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
+    }
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "vk_device_error");
+    *out_word = w;
+    return VK_OK;
+}
+
+extern "C" int vk_selftest_wait_timeout(int device, int64_t timeout_us)
+{
+    if (timeout_us <= 0 || timeout_us > 10000000) return set_error(VK_ERR_INVALID_ARGUMENT, "timeout_us out of range");
+    int prev = 0;
+    VK_CUDA_TRY(cudaGetDevice(&prev));
+    VK_CUDA_TRY(cudaSetDevice(device));
+    int dev = 0;
+    int rc = current_device(&dev, nullptr);
+    if (rc != VK_OK) {
+        cudaSetDevice(prev);
+        return rc;
+    }
+    const unsigned long long z = 0;
+    unsigned long long w = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
+    if (e == cudaSuccess) {
+        selftest_wait_kernel<<<1, 32>>>(static_cast<unsigned long long>(timeout_us) * 1000ull);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&w, g_device_error, sizeof(w));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "vk_selftest_wait_timeout");
+    if ((w >> 32) == kErrWaitSelftest)
+        return set_error(VK_ERR_DEVICE_TIMEOUT, "self-test wait ran out after %lld us as designed",
+                         (long long)timeout_us);
+    return set_error(VK_ERR_CUDA, "self-test wait did not report a timeout (word=%llx)", w);
+}
