@@ -135,6 +135,14 @@ int vk_selftest_wait_timeout(int device, int64_t timeout_us);
 /* Per-call device-side wait limit for the GEMM kernels, nanoseconds (default 2e9). */
 int vk_set_wait_timeout_ns(uint64_t ns);
 
+/* Process-wide tuning knobs (no counterpart in the reference, whose versions hard-code them):
+ *   "tail_split"      1 (default) = cut the tiles of a partial last wave into k-slices, 0 = off
+ *   "raster_group"    tiles along M per rasterisation group of the persistent scheduler (8)
+ *   "stages_2sm256"   shared-memory pipeline depth of the 256-column pair kernel (6 or 7)
+ *   "wait_timeout_ns" same as vk_set_wait_timeout_ns
+ * Returns VK_ERR_INVALID_ARGUMENT for an unknown name or value. */
+int vk_set_option(const char* name, int64_t value);
+
 #ifdef __cplusplus
 }
 #endif

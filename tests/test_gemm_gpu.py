@@ -79,8 +79,9 @@ def test_fp16acc_1024(vk, algo, tile_n):
     _, g32 = v0.v0_f16(A, B)
     assert not np.isnan(c32).any()
     assert v0.rel_frobenius(c16.astype(np.float32), g32) <= FROB_F16ACC
-    # the fp32 copy of an fp16-accumulated result is its exact widening
-    assert np.array_equal(c16.astype(np.float32), c32)
+    # the fp16 output is the round-to-nearest of the fp32 copy (the copy is the exact widening of
+    # the fp16 accumulator, or the fp32 sum of k-slices when the tail split cut the tile)
+    assert np.array_equal(c32.astype(np.float16).view(np.uint16), c16.view(np.uint16))
 
 
 def test_cfg1_rubric_4096_seed1(vk):
@@ -187,20 +188,62 @@ def test_canary_and_strides(vk, dtype):
     assert v0.max_elem_rel(out[1:m + 1, 8:8 + n], g) <= ELEM
 
 
-def test_repeated_launches_are_bitwise_identical(vk):
-    """The reference's race check: 110 consecutive launches compared (10 warm-up + 100)."""
-    A, B = v0.make_inputs(2048, 2048, 2048, 51)
+# (2048^3: 64 whole tiles, no split) (1024x1024x2048: 16 tiles cut into 4 k-slices)
+# (4096x4096x1024: 3 full waves + 34 tiles cut into 2 k-slices)
+@pytest.mark.parametrize("shape", [(2048, 2048, 2048), (1024, 1024, 2048), (4096, 4096, 1024)])
+@pytest.mark.parametrize("acc", ["f32", "f16"])
+def test_repeated_launches_are_bitwise_identical(vk, shape, acc):
+    """The reference's race check: 110 consecutive launches compared (10 warm-up + 100).
+    With the tail split this also proves the arrival counters return to zero every launch."""
+    m, n, k = shape
+    A, B = v0.make_inputs(m, n, k, 51, lo=-0.5, hi=0.5)
     dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
-    first = vk.gemm(dA, dB).clone()
+    first = vk.gemm(dA, dB, acc=acc).clone()
     C = torch.empty_like(first)
     mismatches = 0
     for _ in range(110):
         C.fill_(float("nan"))
-        vk.gemm(dA, dB, C)
+        vk.gemm(dA, dB, C, acc=acc)
         mismatches += int(not torch.equal(C.view(torch.int16), first.view(torch.int16)))
     torch.cuda.synchronize()
     assert mismatches == 0
     assert vk.device_error(0) == 0
+    g32 = v0.v0_f16(A, B)[1]
+    tol = FROB_F32ACC if acc == "f32" else FROB_F16ACC
+    assert v0.rel_frobenius(first.cpu().numpy().astype(np.float32), g32) <= max(tol, 5e-4)
+
+
+@pytest.mark.parametrize("shape", [(1024, 1024, 1024), (4096, 4096, 4096), (4000, 5120, 3000), (300, 200, 4096)])
+def test_tail_split_matches_unsplit(vk, shape):
+    """Tail split on (default) and off give results within the fp32-accumulate tolerance."""
+    m, n, k = shape
+    A, B = v0.make_inputs(m, n, k, 52)
+    try:
+        vk.set_option("tail_split", 0)
+        c16_off, c32_off = _run16(vk, A, B)
+    finally:
+        vk.set_option("tail_split", 1)
+    c16_on, c32_on = _run16(vk, A, B)
+    g32 = v0.v0_f16(A, B)[1]
+    for c in (c32_off, c32_on):
+        assert v0.rel_frobenius(c, g32) <= FROB_F32ACC
+        assert v0.max_elem_rel(c, g32) <= ELEM
+
+
+def test_seven_stage_pair_kernel(vk):
+    A, B = v0.make_inputs(1024, 2048, 1536, 53)
+    try:
+        vk.set_option("stages_2sm256", 7)
+        c16, c32 = _run16(vk, A, B, algo="tc2", tile_n=256)
+    finally:
+        vk.set_option("stages_2sm256", 6)
+    _check_f32acc(c16, c32, A, B)
+
+
+def test_options_reject_bad_values(vk):
+    for name, val in [("raster_group", 0), ("stages_2sm256", 5), ("nope", 1)]:
+        with pytest.raises(vk.VkError):
+            vk.set_option(name, val)
 
 
 def test_k_zero_and_empty(vk):

@@ -38,7 +38,7 @@ _ACCS = {"f32": ACC_F32, "f16": ACC_F16}
 EXPORTED = (
     "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
-    "vk_set_wait_timeout_ns",
+    "vk_set_wait_timeout_ns", "vk_set_option",
 )
 
 
@@ -72,7 +72,7 @@ class ShardArgs(ctypes.Structure):
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is not built; run `python -m vibekernel_b200.build` (nvcc, sm_100a). "
+            f"{LIB_PATH} is not built; run `python vibekernel_b200/build.py` (nvcc, sm_100a). "
             "There is no CPU fallback.")
     lib = ctypes.CDLL(LIB_PATH)
     lib.vk_gemm.argtypes = [ctypes.POINTER(GemmArgs)]
@@ -98,6 +98,8 @@ def _load() -> ctypes.CDLL:
     lib.vk_selftest_wait_timeout.restype = ctypes.c_int
     lib.vk_set_wait_timeout_ns.argtypes = [ctypes.c_uint64]
     lib.vk_set_wait_timeout_ns.restype = ctypes.c_int
+    lib.vk_set_option.argtypes = [ctypes.c_char_p, ctypes.c_int64]
+    lib.vk_set_option.restype = ctypes.c_int
     return lib
 
 
@@ -195,6 +197,11 @@ def device_error(device: int = 0, clear: bool = True) -> int:
     w = ctypes.c_uint64(0)
     check(lib.vk_device_error(device, ctypes.byref(w), 1 if clear else 0))
     return int(w.value)
+
+
+def set_option(name: str, value: int) -> None:
+    """Process-wide knob: tail_split, raster_group, stages_2sm256, wait_timeout_ns."""
+    check(lib.vk_set_option(name.encode(), int(value)))
 
 
 def set_wait_timeout_ns(ns: int) -> None:

@@ -1,6 +1,8 @@
 """Build libvkgemm.so in-tree for sm_100a (nvcc cross-compiles; no GPU needed).
 
-    python -m vibekernel_b200.build [--verbose]
+    python vibekernel_b200/build.py [--verbose]
+
+(run it as a script: importing the package first would load a stale library).
 
 The library is one shared object with a plain C ABI (include/vkgemm.h).  It links the CUDA
 runtime statically; NCCL is opened lazily (dlopen) by the sharded layer only.

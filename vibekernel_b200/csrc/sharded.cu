@@ -239,5 +239,6 @@ extern "C" int vk_shutdown(void)
     }
     g_groups.clear();
     cudaSetDevice(prev);
+    vk::release_device_state();
     return VK_OK;
 }

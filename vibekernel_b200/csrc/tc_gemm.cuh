@@ -23,6 +23,15 @@
 //
 // Ragged shapes: TMA zero-fills out-of-range rows/columns of A and B (M, N and the K tail);
 // the epilogue predicates stores on row < M and col < N.
+//
+// Tail split (the reference's last-wave K-split, results/ralph_loop_fable/src/matmul_f16/
+// matmul_f16_v23_wavesplit.cu:1-8 and matmul_f16_v42_shfl2.cu:182-189): with T tiles on C
+// persistent clusters, the first F*C tiles (F = T / C full waves) run whole; each of the R = T - F*C
+// tiles of the partial last wave is cut into S = C / R k-slices, so the last wave takes ~1/S of a
+// tile.  Every slice writes its fp32 partial to a workspace and bumps a per-(tile, CTA, warp)
+// arrival counter; the slice that arrives last adds the others' partials to its own accumulator
+// and writes C, then resets the counter.  Nobody waits on another CTA, so the tail cannot
+// deadlock whatever the residency.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -40,7 +49,35 @@ struct TcParams {
     float* C32;              // optional fp32 copy, ld = N
     int vec_ok;              // C / C32 alignment allows 16-byte stores
     unsigned long long timeout_ns;
+    // work units: [0, full_units) are whole tiles, then (units - full_units) / split tail tiles
+    // cut into `split` k-slices each
+    int units, full_units, split;
+    float* ws;               // split partials: [tail tile][slice][CTA rank][128 rows x BN] fp32
+    int* counters;           // arrival counters: [tail tile][CTA rank][4 epilogue warps]
 };
+
+struct Unit {
+    int tile, kb0, kb1, slice;  // slice < 0: whole tile
+};
+
+__device__ __forceinline__ Unit unit_info(const TcParams& p, int u)
+{
+    Unit w;
+    if (u < p.full_units) {
+        w.tile = u;
+        w.kb0 = 0;
+        w.kb1 = p.num_kb;
+        w.slice = -1;
+    } else {
+        const int v = u - p.full_units;
+        const int ti = v / p.split;
+        w.slice = v - ti * p.split;
+        w.tile = p.full_units + ti;
+        w.kb0 = p.num_kb * w.slice / p.split;
+        w.kb1 = p.num_kb * (w.slice + 1) / p.split;
+    }
+    return w;
+}
 
 template <int CG, int BN, int STAGES, bool ACC_F32>
 struct TcCfg {
@@ -169,7 +206,6 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
     const int cluster_id = blockIdx.x / CG;
     const int num_clusters = gridDim.x / CG;
-    const int num_tiles = p.tiles_m * p.tiles_n;
 
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmap_a);
@@ -200,12 +236,13 @@ __global__ void __launch_bounds__(192, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+            for (int u = cluster_id; ok && u < p.units; u += num_clusters) {
+                const Unit w = unit_info(p, u);
                 int tm, tn;
-                tile_coords(t, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
+                tile_coords(w.tile, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
                 const int m0 = tm * (BM * CG) + static_cast<int>(rank) * BM;
                 const int n0 = tn * BN + static_cast<int>(rank) * Cfg::kBNCta;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, kErrWaitProducer, stage)) {
                         ok = false;
                         break;
@@ -257,13 +294,14 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t phase = 0;
             int it = 0;
             bool ok = true;
-            for (int t = cluster_id; ok && t < num_tiles; t += num_clusters, ++it) {
+            for (int u = cluster_id; ok && u < p.units; u += num_clusters, ++it) {
+                const Unit w = unit_info(p, u);
                 const int acc = it & 1;
                 const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
                 if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, kErrWaitMma, 100 + acc)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, kErrWaitMma, stage)) {
                         ok = false;
                         break;
@@ -275,7 +313,7 @@ __global__ void __launch_bounds__(192, 1)
                     for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
                         const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
                         const uint64_t b_desc = smem_desc_sw128(b_addr + kk * 16 * 128, kBLbo, 1024);
-                        umma_f16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+                        umma_f16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
                     }
                     const uint32_t eb = empty_bar(stage);
                     umma_commit<CG>(eb);
@@ -295,22 +333,98 @@ __global__ void __launch_bounds__(192, 1)
         // ------------------------------------------------------------------ epilogue
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         int it = 0;
-        for (int t = cluster_id; t < num_tiles; t += num_clusters, ++it) {
+        for (int u = cluster_id; u < p.units; u += num_clusters, ++it) {
+            const Unit w = unit_info(p, u);
             const int acc = it & 1;
             const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
             if (!mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, kErrWaitEpilogue, acc)) break;
             tc_fence_after();
             int tm, tn;
-            tile_coords(t, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
+            tile_coords(w.tile, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
             const int row = tm * (BM * CG) + static_cast<int>(rank) * BM + q * 32 + lane;
             const int col0 = tn * BN;
             const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+            if (w.slice >= 0) {
+                // Tail slice: publish this slice's fp32 partial (lane-major float4 runs, so each warp
+                // store is one contiguous 512-byte span), then count arrivals; only the last slice
+                // to arrive reduces and writes C.
+                const int ti = w.tile - p.full_units;
+                constexpr size_t kRegion = static_cast<size_t>(BM) * BN;
+                const size_t warp_off = static_cast<size_t>(q) * 32 * BN;
+                float* mine = p.ws + (static_cast<size_t>(ti * p.split + w.slice) * CG + rank) * kRegion + warp_off;
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
-                tmem_ld_wait();
-                if (col0 + c < p.N) store_chunk<ACC_F32>(p, row, col0 + c, r);
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
+                    tmem_ld_wait();
+                    float4* dst = reinterpret_cast<float4*>(mine + c * 32);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        float4 f;
+                        if constexpr (ACC_F32) {
+                            f = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+                        } else {
+                            f = make_float4(__half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j]))),
+                                            __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 1]))),
+                                            __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 2]))),
+                                            __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 3]))));
+                        }
+                        __stcg(dst + j * 32 + lane, f);
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                int* ctr = p.counters + (ti * CG + static_cast<int>(rank)) * 4 + q;
+                int old = 0;
+                if (lane == 0) old = atomicAdd(ctr, 1);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == p.split - 1) {
+                    __threadfence();
+#pragma unroll 1
+                    for (int c = 0; c < BN; c += 32) {
+                        if (col0 + c >= p.N) break;
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
+                        tmem_ld_wait();
+                        float f[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if constexpr (ACC_F32)
+                                f[i] = __uint_as_float(r[i]);
+                            else
+                                f[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(r[i])));
+                        }
+#pragma unroll 1
+                        for (int s2 = 0; s2 < p.split; ++s2) {
+                            if (s2 == w.slice) continue;
+                            const float4* src = reinterpret_cast<const float4*>(
+                                p.ws + (static_cast<size_t>(ti * p.split + s2) * CG + rank) * kRegion + warp_off + c * 32);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                const float4 v = __ldcg(src + j * 32 + lane);
+                                f[4 * j] += v.x;
+                                f[4 * j + 1] += v.y;
+                                f[4 * j + 2] += v.z;
+                                f[4 * j + 3] += v.w;
+                            }
+                        }
+                        // the k-slices are summed in fp32 in both tiers
+                        uint32_t rr[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(f[i]);
+                        store_chunk<true>(p, row, col0 + c, rr);
+                    }
+                    if (lane == 0) *ctr = 0;  // every slice has arrived: ready for the next launch
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
+                    tmem_ld_wait();
+                    if (col0 + c < p.N) store_chunk<ACC_F32>(p, row, col0 + c, r);
+                }
             }
             tc_fence_before();
             __syncwarp();

@@ -4,4 +4,6 @@
 namespace vk {
 // Records a thread-local error message (read back by vk_last_error_string) and returns `code`.
 int set_error(int code, const char* fmt, ...);
+// Frees per-device scratch owned by the library (vk_shutdown).
+void release_device_state();
 }  // namespace vk

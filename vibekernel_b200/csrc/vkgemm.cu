@@ -78,11 +78,20 @@ struct DeviceState {
     int sm_count = 0;
     KernelSlot kernels[kMaxKernels];
     int num_kernels = 0;
+    // Tail-split scratch, allocated once on first need: fp32 partials for at most one unit per
+    // persistent CTA (sm_count x 128 x 256 floats, 19.4 MB on 148 SMs) and 4 arrival counters
+    // per CTA (zeroed at allocation; each reduction leaves them zero again).
+    float* ws = nullptr;
+    int* counters = nullptr;
+    size_t ws_bytes = 0, ctr_bytes = 0;
 };
 
 static std::mutex g_mu;
 static DeviceState g_dev[kMaxDevices];
 static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+static std::atomic<int> g_tail_split{1};
+static std::atomic<int> g_raster_group{8};
+static std::atomic<int> g_stages_2sm256{6};
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -176,6 +185,62 @@ static int kernel_slot(DeviceState& st, Kernel fn, int smem, int threads, int cl
     return VK_OK;
 }
 
+// Tail-split workspace for the current device (allocated once; see DeviceState).
+static int ensure_workspace(DeviceState& st, int dev)
+{
+    if (st.ws != nullptr) return VK_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (st.ws != nullptr) return VK_OK;
+    const size_t ws_bytes = static_cast<size_t>(st.sm_count) * 128 * 256 * sizeof(float);
+    const size_t ctr_bytes = static_cast<size_t>(st.sm_count) * 4 * sizeof(int);
+    float* ws = nullptr;
+    int* ctr = nullptr;
+    cudaError_t e = cudaMalloc(&ws, ws_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&ctr, ctr_bytes);
+    if (e == cudaSuccess) e = cudaMemset(ctr, 0, ctr_bytes);
+    if (e != cudaSuccess) {
+        if (ws) cudaFree(ws);
+        if (ctr) cudaFree(ctr);
+        return set_error(VK_ERR_CUDA, "tail-split workspace on device %d: %s", dev, cudaGetErrorString(e));
+    }
+    st.ctr_bytes = ctr_bytes;
+    st.ws_bytes = ws_bytes;
+    st.counters = ctr;
+    st.ws = ws;
+    return VK_OK;
+}
+
+// Work decomposition of the persistent tensor-core kernels: whole tiles for the full waves,
+// and the tiles of a partial last wave cut into k-slices (at least kMinSliceKb k-blocks each).
+struct Schedule {
+    int units, full_units, split, grid_units;
+};
+
+static constexpr int kMinSliceKb = 4;
+
+static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool allow_split)
+{
+    Schedule sc;
+    sc.units = static_cast<int>(tiles);
+    sc.full_units = static_cast<int>(tiles);
+    sc.split = 1;
+    if (allow_split && tiles > 0) {
+        const long long full_waves = tiles / max_units;
+        const long long rem = tiles - full_waves * max_units;
+        if (rem > 0) {
+            long long s = max_units / rem;
+            if (s > num_kb / kMinSliceKb) s = num_kb / kMinSliceKb;
+            if (s >= 2) {
+                sc.full_units = static_cast<int>(full_waves * max_units);
+                sc.split = static_cast<int>(s);
+                sc.units = static_cast<int>(sc.full_units + rem * s);
+            }
+        }
+    }
+    sc.grid_units = sc.units < max_units ? sc.units : max_units;
+    return sc;
+}
+
 // ------------------------------------------------------------------------------------------
 // Tensor maps
 // ------------------------------------------------------------------------------------------
@@ -211,7 +276,7 @@ struct Problem {
 };
 
 template <int CG, int BN, int STAGES, bool ACC_F32>
-static int launch_tc(DeviceState& st, const Problem& pb)
+static int launch_tc(DeviceState& st, int dev, const Problem& pb)
 {
     using Cfg = TcCfg<CG, BN, STAGES, ACC_F32>;
     auto fn = tc_gemm_kernel<CG, BN, STAGES, ACC_F32>;
@@ -232,7 +297,7 @@ static int launch_tc(DeviceState& st, const Problem& pb)
     p.tiles_m = static_cast<int>((pb.m + Cfg::kBM * CG - 1) / (Cfg::kBM * CG));
     p.tiles_n = static_cast<int>((pb.n + BN - 1) / BN);
     p.num_kb = static_cast<int>((pb.k + Cfg::kBK - 1) / Cfg::kBK);
-    p.raster_group = 8;
+    p.raster_group = g_raster_group.load(std::memory_order_relaxed);
     p.C = static_cast<__half*>(pb.C);
     p.ldc = pb.ldc;
     p.C32 = pb.C32;
@@ -242,7 +307,19 @@ static int launch_tc(DeviceState& st, const Problem& pb)
     p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-    const int clusters = static_cast<int>(tiles < max_units ? tiles : max_units);
+    const Schedule sc = plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0);
+    p.units = sc.units;
+    p.full_units = sc.full_units;
+    p.split = sc.split;
+    p.ws = nullptr;
+    p.counters = nullptr;
+    if (sc.split > 1) {
+        rc = ensure_workspace(st, dev);
+        if (rc != VK_OK) return rc;
+        p.ws = st.ws;
+        p.counters = st.counters;
+    }
+    const int clusters = sc.grid_units;
 
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -319,6 +396,27 @@ static bool tma_ok_f16(const void* p, int64_t ld)
     return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && ((ld * 2) % 16 == 0) && (ld * 2 < (1LL << 40));
 }
 
+int dispatch(DeviceState& st, int dev, const Problem& pb, int dtype, int acc, int algo);
+
+// Frees every device's tail-split workspace (called from vk_shutdown).
+void release_device_state()
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    for (int d = 0; d < kMaxDevices; ++d) {
+        DeviceState& st = g_dev[d];
+        if (st.ws == nullptr) continue;
+        cudaSetDevice(d);
+        cudaFree(st.ws);
+        cudaFree(st.counters);
+        st.ws = nullptr;
+        st.counters = nullptr;
+        st.ws_bytes = st.ctr_bytes = 0;
+    }
+    cudaSetDevice(prev);
+}
+
 }  // namespace vk
 
 // ==========================================================================================
@@ -368,25 +466,31 @@ extern "C" int vk_gemm(const vk_gemm_args* a)
     DeviceState* st = nullptr;
     int rc = current_device(&dev, &st);
     if (rc != VK_OK) return rc;
+    return dispatch(*st, dev, pb, a->dtype, a->acc, a->algo);
+}
 
+namespace vk {
+int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc, int algo_in)
+{
+    DeviceState* st = &st_ref;
     if (pb.m == 0 || pb.n == 0) return VK_OK;
     if (pb.C == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: C is NULL");
-    if (pb.k == 0) return a->dtype == VK_DTYPE_F16 ? launch_zero<__half>(*st, pb) : launch_zero<float>(*st, pb);
+    if (pb.k == 0) return dtype == VK_DTYPE_F16 ? launch_zero<__half>(*st, pb) : launch_zero<float>(*st, pb);
     if (pb.A == nullptr || pb.B == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: A or B is NULL");
 
-    if (a->dtype == VK_DTYPE_F32) {
-        if (a->algo != VK_ALGO_AUTO && a->algo != VK_ALGO_FFMA)
+    if (dtype == VK_DTYPE_F32) {
+        if (algo_in != VK_ALGO_AUTO && algo_in != VK_ALGO_FFMA)
             return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: fp32 runs on the FFMA kernel only");
         return launch_sgemm(pb);
     }
 
     // fp16
     const bool tma_ok = tma_ok_f16(pb.A, pb.lda) && tma_ok_f16(pb.B, pb.ldb);
-    int algo = a->algo;
+    int algo = algo_in;
     if (algo == VK_ALGO_FFMA) return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: FFMA kernel is fp32 only");
     if (algo == VK_ALGO_AUTO) algo = tma_ok ? VK_ALGO_TC_2SM : VK_ALGO_SIMT;
     if (algo == VK_ALGO_SIMT) {
-        if (a->acc != VK_ACC_F32)
+        if (acc != VK_ACC_F32)
             return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: the predicated CUDA-core kernel accumulates in fp32 only");
         return launch_hgemm_simt(pb);
     }
@@ -395,14 +499,19 @@ extern "C" int vk_gemm(const vk_gemm_args* a)
                          "vk_gemm: tensor-core kernels need 16-byte aligned A/B and lda, ldb multiples of 8 "
                          "(use VK_ALGO_AUTO or VK_ALGO_SIMT)");
     const int tn = pb.tile_n ? pb.tile_n : 256;
-    const bool f32 = a->acc == VK_ACC_F32;
+    const bool f32 = acc == VK_ACC_F32;
     if (algo == VK_ALGO_TC_2SM) {
-        if (tn == 256) return f32 ? launch_tc<2, 256, 6, true>(*st, pb) : launch_tc<2, 256, 6, false>(*st, pb);
-        return f32 ? launch_tc<2, 128, 8, true>(*st, pb) : launch_tc<2, 128, 8, false>(*st, pb);
+        if (tn == 256) {
+            if (g_stages_2sm256.load(std::memory_order_relaxed) == 7)
+                return f32 ? launch_tc<2, 256, 7, true>(*st, dev, pb) : launch_tc<2, 256, 7, false>(*st, dev, pb);
+            return f32 ? launch_tc<2, 256, 6, true>(*st, dev, pb) : launch_tc<2, 256, 6, false>(*st, dev, pb);
+        }
+        return f32 ? launch_tc<2, 128, 8, true>(*st, dev, pb) : launch_tc<2, 128, 8, false>(*st, dev, pb);
     }
-    if (tn == 256) return f32 ? launch_tc<1, 256, 4, true>(*st, pb) : launch_tc<1, 256, 4, false>(*st, pb);
-    return f32 ? launch_tc<1, 128, 6, true>(*st, pb) : launch_tc<1, 128, 6, false>(*st, pb);
+    if (tn == 256) return f32 ? launch_tc<1, 256, 4, true>(*st, dev, pb) : launch_tc<1, 256, 4, false>(*st, dev, pb);
+    return f32 ? launch_tc<1, 128, 6, true>(*st, dev, pb) : launch_tc<1, 128, 6, false>(*st, dev, pb);
 }
+}  // namespace vk
 
 extern "C" int vk_matmul_f16(int version, size_t m, size_t n, size_t k, const void* A, const void* B, void* C)
 {
@@ -461,6 +570,31 @@ extern "C" const char* vk_last_error_string(void) { return t_last_error.c_str();
 
 extern "C" const char* vk_version_string(void) { return "vkgemm 0.1.0 (sm_100a)"; }
 
+extern "C" int vk_set_option(const char* name, int64_t value)
+{
+    if (name == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_set_option: name is NULL");
+    if (strcmp(name, "tail_split") == 0) {
+        g_tail_split.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
+    if (strcmp(name, "raster_group") == 0) {
+        if (value < 1 || value > 64) return set_error(VK_ERR_INVALID_ARGUMENT, "raster_group must be 1..64");
+        g_raster_group.store(static_cast<int>(value));
+        return VK_OK;
+    }
+    if (strcmp(name, "stages_2sm256") == 0) {
+        if (value != 6 && value != 7) return set_error(VK_ERR_INVALID_ARGUMENT, "stages_2sm256 must be 6 or 7");
+        g_stages_2sm256.store(static_cast<int>(value));
+        return VK_OK;
+    }
+    if (strcmp(name, "wait_timeout_ns") == 0) {
+        if (value <= 0) return set_error(VK_ERR_INVALID_ARGUMENT, "wait_timeout_ns must be > 0");
+        g_timeout_ns.store(static_cast<unsigned long long>(value));
+        return VK_OK;
+    }
+    return set_error(VK_ERR_INVALID_ARGUMENT, "vk_set_option: unknown option '%s'", name);
+}
+
 extern "C" int vk_set_wait_timeout_ns(uint64_t ns)
 {
     if (ns == 0) return set_error(VK_ERR_INVALID_ARGUMENT, "timeout must be > 0");
@@ -480,6 +614,9 @@ extern "C" int vk_device_error(int device, uint64_t* out_word, int clear)
     if (e == cudaSuccess && clear && w != 0) {
         const unsigned long long z = 0;
         e = cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
+        // a kernel that gave up may have left tail-split arrival counters mid-count
+        if (e == cudaSuccess && device >= 0 && device < kMaxDevices && g_dev[device].counters != nullptr)
+            e = cudaMemset(g_dev[device].counters, 0, g_dev[device].ctr_bytes);
     }
     cudaSetDevice(prev);
     if (e != cudaSuccess) return cuda_fail(e, "vk_device_error");
