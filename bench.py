@@ -261,6 +261,10 @@ def main():
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     evg = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
+    probe = dt == "f16"  # the tensor-core kernels carry the in-kernel clock probe
+    if probe:
+        vk.set_option("clock_probe", 1)
+        vk.read_clock_probe(local, clear=True)
     with ClockSampler(local) as clocks:
         for i in range(args.steps):
             flush.fill_(1.0)
@@ -272,6 +276,10 @@ def main():
             evg[i][1].record(stream)
             ev[i][1].synchronize()  # the reference driver synchronises every iteration
         barrier()
+    kernel_mhz = None
+    if probe:
+        kernel_mhz, _ = vk.read_clock_probe(local, clear=True)
+        vk.set_option("clock_probe", 0)
     gemm_ms = sum(s.elapsed_time(e) for s, e in ev)
     gather_ms = sum(s.elapsed_time(e) for s, e in evg) if C_full is not None else 0.0
     err = vk.device_error(local)
@@ -348,7 +356,9 @@ def main():
                        "timing": "per-call CUDA events + event synchronize (reference main.cpp loop)"},
             "roofline": roof,
             "pct_of_dense_peak_2250": round(value / world / 2250.0, 4),
-            "clocks": clocks.summary(),
+            "clocks": dict(clocks.summary(), kernel_sm_mhz=(round(kernel_mhz, 1) if kernel_mhz else None)),
+            "clock_true_peak_frac": (round(achieved / (148 * 8192 * kernel_mhz * 1e6 / 1e12), 4)
+                                     if (kernel_mhz and dt == "f16") else None),
             "gpu_launches": args.steps,
             "e2e": e2e,
         }

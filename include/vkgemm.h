@@ -140,8 +140,15 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *   "raster_group"    tiles along M per rasterisation group of the persistent scheduler (8)
  *   "stages_2sm256"   shared-memory pipeline depth of the 256-column pair kernel (6 or 7)
  *   "wait_timeout_ns" same as vk_set_wait_timeout_ns
+ *   "clock_probe"     1 = the tensor-core kernels accumulate the SM cycles and nanoseconds of
+ *                     their first CTA (read with vk_read_clock_probe); 0 (default) = off
  * Returns VK_ERR_INVALID_ARGUMENT for an unknown name or value. */
 int vk_set_option(const char* name, int64_t value);
+
+/* Clock probe (no counterpart in the reference, whose scores were confounded by the unlogged
+ * SM clock, README.md:160): out3 = {SM cycles, nanoseconds, launches} accumulated since the last
+ * clear; cycles / ns is the SM clock in GHz that the kernels actually ran at.  Synchronises. */
+int vk_read_clock_probe(int device, uint64_t* out3, int clear);
 
 #ifdef __cplusplus
 }

@@ -38,7 +38,7 @@ _ACCS = {"f32": ACC_F32, "f16": ACC_F16}
 EXPORTED = (
     "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
-    "vk_set_wait_timeout_ns", "vk_set_option",
+    "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe",
 )
 
 
@@ -100,6 +100,8 @@ def _load() -> ctypes.CDLL:
     lib.vk_set_wait_timeout_ns.restype = ctypes.c_int
     lib.vk_set_option.argtypes = [ctypes.c_char_p, ctypes.c_int64]
     lib.vk_set_option.restype = ctypes.c_int
+    lib.vk_read_clock_probe.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]
+    lib.vk_read_clock_probe.restype = ctypes.c_int
     return lib
 
 
@@ -202,6 +204,14 @@ def device_error(device: int = 0, clear: bool = True) -> int:
 def set_option(name: str, value: int) -> None:
     """Process-wide knob: tail_split, raster_group, stages_2sm256, wait_timeout_ns."""
     check(lib.vk_set_option(name.encode(), int(value)))
+
+
+def read_clock_probe(device: int = 0, clear: bool = True):
+    """Returns (sm_mhz, launches) measured inside the tensor-core kernels since the last clear."""
+    out = (ctypes.c_uint64 * 3)()
+    check(lib.vk_read_clock_probe(device, out, 1 if clear else 0))
+    cycles, ns, launches = int(out[0]), int(out[1]), int(out[2])
+    return (cycles / ns * 1e3 if ns else None), launches
 
 
 def set_wait_timeout_ns(ns: int) -> None:

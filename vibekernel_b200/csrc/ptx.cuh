@@ -16,6 +16,9 @@ namespace vk {
 // ------------------------------------------------------------------------------------------
 __device__ unsigned long long g_device_error = 0ull;
 
+// Clock probe accumulators: [0] SM cycles, [1] nanoseconds, [2] launches (see vk_read_clock_probe).
+__device__ unsigned long long g_clock_probe[3] = {0ull, 0ull, 0ull};
+
 enum : uint32_t {
     kErrWaitProducer = 1,   // producer gave up waiting for a free stage
     kErrWaitMma = 2,        // MMA issuer gave up waiting for a loaded stage / free accumulator
@@ -107,7 +110,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(bar), "r"(parity)

@@ -29,9 +29,10 @@
 // persistent clusters, the first F*C tiles (F = T / C full waves) run whole; each of the R = T - F*C
 // tiles of the partial last wave is cut into S = C / R k-slices, so the last wave takes ~1/S of a
 // tile.  Every slice writes its fp32 partial to a workspace and bumps a per-(tile, CTA, warp)
-// arrival counter; the slice that arrives last adds the others' partials to its own accumulator
-// and writes C, then resets the counter.  Nobody waits on another CTA, so the tail cannot
-// deadlock whatever the residency.
+// arrival counter; the slice that arrives last sums all slices in slice order (its own from TMEM,
+// the others from the workspace) -- the same order whoever arrives last, so results are
+// bitwise reproducible -- writes C, and resets the counter.  Nobody waits on another CTA, so
+// the tail cannot deadlock whatever the residency.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -54,6 +55,7 @@ struct TcParams {
     int units, full_units, split;
     float* ws;               // split partials: [tail tile][slice][CTA rank][128 rows x BN] fp32
     int* counters;           // arrival counters: [tail tile][CTA rank][4 epilogue warps]
+    int clock_probe;         // 1: CTA 0 accumulates (cycles, ns, launches) into g_clock_probe
 };
 
 struct Unit {
@@ -229,6 +231,11 @@ __global__ void __launch_bounds__(192, 1)
     if constexpr (CG == 2) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    uint64_t probe_t0 = 0, probe_c0 = 0;
+    if (p.clock_probe && blockIdx.x == 0 && threadIdx.x == 0) {
+        probe_t0 = globaltimer_ns();
+        probe_c0 = clock64();
+    }
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -387,29 +394,48 @@ __global__ void __launch_bounds__(192, 1)
                         uint32_t r[32];
                         tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
                         tmem_ld_wait();
-                        float f[32];
+                        float own[32];
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             if constexpr (ACC_F32)
-                                f[i] = __uint_as_float(r[i]);
+                                own[i] = __uint_as_float(r[i]);
                             else
-                                f[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(r[i])));
+                                own[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(r[i])));
                         }
+                        // f = ((p_0 + p_1) + p_2) + ... in slice order, p_own taken from TMEM
+                        float f[32];
 #pragma unroll 1
                         for (int s2 = 0; s2 < p.split; ++s2) {
-                            if (s2 == w.slice) continue;
-                            const float4* src = reinterpret_cast<const float4*>(
-                                p.ws + (static_cast<size_t>(ti * p.split + s2) * CG + rank) * kRegion + warp_off + c * 32);
+                            float4 v[8];
+                            if (s2 == w.slice) {
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                const float4 v = __ldcg(src + j * 32 + lane);
-                                f[4 * j] += v.x;
-                                f[4 * j + 1] += v.y;
-                                f[4 * j + 2] += v.z;
-                                f[4 * j + 3] += v.w;
+                                for (int j = 0; j < 8; ++j)
+                                    v[j] = make_float4(own[4 * j], own[4 * j + 1], own[4 * j + 2], own[4 * j + 3]);
+                            } else {
+                                const float4* src = reinterpret_cast<const float4*>(
+                                    p.ws + (static_cast<size_t>(ti * p.split + s2) * CG + rank) * kRegion + warp_off +
+                                    c * 32);
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + j * 32 + lane);
+                            }
+                            if (s2 == 0) {
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) {
+                                    f[4 * j] = v[j].x;
+                                    f[4 * j + 1] = v[j].y;
+                                    f[4 * j + 2] = v[j].z;
+                                    f[4 * j + 3] = v[j].w;
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) {
+                                    f[4 * j] += v[j].x;
+                                    f[4 * j + 1] += v[j].y;
+                                    f[4 * j + 2] += v[j].z;
+                                    f[4 * j + 3] += v[j].w;
+                                }
                             }
                         }
-                        // the k-slices are summed in fp32 in both tiers
                         uint32_t rr[32];
 #pragma unroll
                         for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(f[i]);
@@ -439,6 +465,13 @@ __global__ void __launch_bounds__(192, 1)
 
     tc_fence_before();
     __syncthreads();
+    if (p.clock_probe && blockIdx.x == 0 && threadIdx.x == 0) {
+        // SM cycles and wall nanoseconds of CTA 0's persistent loop: their ratio is the SM clock
+        // the kernel actually ran at (power capping moves it within a launch).
+        atomicAdd(&g_clock_probe[0], static_cast<unsigned long long>(clock64() - probe_c0));
+        atomicAdd(&g_clock_probe[1], static_cast<unsigned long long>(globaltimer_ns() - probe_t0));
+        atomicAdd(&g_clock_probe[2], 1ull);
+    }
     if constexpr (CG == 2) cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();

@@ -92,6 +92,7 @@ static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 static std::atomic<int> g_tail_split{1};
 static std::atomic<int> g_raster_group{8};
 static std::atomic<int> g_stages_2sm256{6};
+static std::atomic<int> g_clock_probe_on{0};
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -305,6 +306,7 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb)
     const bool c32_vec = pb.C32 == nullptr || ((reinterpret_cast<uintptr_t>(pb.C32) % 16 == 0) && (pb.n % 4 == 0));
     p.vec_ok = (c_vec && c32_vec) ? 1 : 0;
     p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
+    p.clock_probe = g_clock_probe_on.load(std::memory_order_relaxed);
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
     const Schedule sc = plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0);
@@ -587,6 +589,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
         g_stages_2sm256.store(static_cast<int>(value));
         return VK_OK;
     }
+    if (strcmp(name, "clock_probe") == 0) {
+        g_clock_probe_on.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
     if (strcmp(name, "wait_timeout_ns") == 0) {
         if (value <= 0) return set_error(VK_ERR_INVALID_ARGUMENT, "wait_timeout_ns must be > 0");
         g_timeout_ns.store(static_cast<unsigned long long>(value));
@@ -621,6 +627,27 @@ extern "C" int vk_device_error(int device, uint64_t* out_word, int clear)
     cudaSetDevice(prev);
     if (e != cudaSuccess) return cuda_fail(e, "vk_device_error");
     *out_word = w;
+    return VK_OK;
+}
+
+extern "C" int vk_read_clock_probe(int device, uint64_t* out3, int clear)
+{
+    if (out3 == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "out3 is NULL");
+    int prev = 0;
+    VK_CUDA_TRY(cudaGetDevice(&prev));
+    VK_CUDA_TRY(cudaSetDevice(device));
+    unsigned long long v[3] = {0, 0, 0};
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(v, g_clock_probe, sizeof(v));
+    if (e == cudaSuccess && clear) {
+        const unsigned long long z[3] = {0, 0, 0};
+        e = cudaMemcpyToSymbol(g_clock_probe, z, sizeof(z));
+    }
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "vk_read_clock_probe");
+    out3[0] = v[0];
+    out3[1] = v[1];
+    out3[2] = v[2];
     return VK_OK;
 }
 
