@@ -142,6 +142,7 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *   "wait_timeout_ns" same as vk_set_wait_timeout_ns
  *   "clock_probe"     1 = the tensor-core kernels accumulate the SM cycles and nanoseconds of
  *                     their first CTA (read with vk_read_clock_probe); 0 (default) = off
+ *   "trace"           1 = the tensor-core kernels record a launch timeline (vk_read_trace)
  * Returns VK_ERR_INVALID_ARGUMENT for an unknown name or value. */
 int vk_set_option(const char* name, int64_t value);
 
@@ -149,6 +150,14 @@ int vk_set_option(const char* name, int64_t value);
  * SM clock, README.md:160): out3 = {SM cycles, nanoseconds, launches} accumulated since the last
  * clear; cycles / ns is the SM clock in GHz that the kernels actually ran at.  Synchronises. */
 int vk_read_clock_probe(int device, uint64_t* out3, int clear);
+
+/* Launch timeline of the last tensor-core launch made with the "trace" option (no counterpart
+ * in the reference), %globaltimer nanoseconds: [0] CTA 0 entry, [1] prologue done, [2] first
+ * TMA issued, [3] first stage full at the MMA issuer, [4] last MMA commit, [5] first accumulator
+ * ready at the epilogue, [6] last epilogue store issued, [7] CTA 0 exit, [8]/[9] earliest/latest
+ * CTA entry, [10]/[11] earliest/latest CTA exit.  Read once, re-arm for the next launch first
+ * (call it once before tracing).  Synchronises. */
+int vk_read_trace(int device, uint64_t* out16);
 
 #ifdef __cplusplus
 }

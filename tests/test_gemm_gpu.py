@@ -190,11 +190,12 @@ def test_canary_and_strides(vk, dtype):
 
 # (2048^3: 64 whole tiles, no split) (1024x1024x2048: 16 tiles cut into 4 k-slices)
 # (4096x4096x1024: 3 full waves + 34 tiles cut into 2 k-slices)
-@pytest.mark.parametrize("shape", [(2048, 2048, 2048), (1024, 1024, 2048), (4096, 4096, 1024)])
+@pytest.mark.parametrize("shape", [(2048, 2048, 2048), (1024, 1024, 2048), (4096, 4096, 1024), (256, 256, 4096)])
 @pytest.mark.parametrize("acc", ["f32", "f16"])
 def test_repeated_launches_are_bitwise_identical(vk, shape, acc):
     """The reference's race check: 110 consecutive launches compared (10 warm-up + 100).
-    With the tail split this also proves the arrival counters return to zero every launch."""
+    With the tail split this also proves the arrival counters return to zero every launch and
+    that the slice sum does not depend on which slice arrives last (256x256x4096: 8 slices)."""
     m, n, k = shape
     A, B = v0.make_inputs(m, n, k, 51, lo=-0.5, hi=0.5)
     dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
@@ -213,7 +214,8 @@ def test_repeated_launches_are_bitwise_identical(vk, shape, acc):
     assert v0.rel_frobenius(first.cpu().numpy().astype(np.float32), g32) <= max(tol, 5e-4)
 
 
-@pytest.mark.parametrize("shape", [(1024, 1024, 1024), (4096, 4096, 4096), (4000, 5120, 3000), (300, 200, 4096)])
+@pytest.mark.parametrize("shape", [(1024, 1024, 1024), (4096, 4096, 4096), (4000, 5120, 3000), (300, 200, 4096),
+                                   (256, 256, 4096), (512, 768, 2048), (700, 1000, 1200)])
 def test_tail_split_matches_unsplit(vk, shape):
     """Tail split on (default) and off give results within the fp32-accumulate tolerance."""
     m, n, k = shape

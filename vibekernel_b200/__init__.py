@@ -38,7 +38,7 @@ _ACCS = {"f32": ACC_F32, "f16": ACC_F16}
 EXPORTED = (
     "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
-    "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe",
+    "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace",
 )
 
 
@@ -102,6 +102,8 @@ def _load() -> ctypes.CDLL:
     lib.vk_set_option.restype = ctypes.c_int
     lib.vk_read_clock_probe.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]
     lib.vk_read_clock_probe.restype = ctypes.c_int
+    lib.vk_read_trace.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint64)]
+    lib.vk_read_trace.restype = ctypes.c_int
     return lib
 
 
@@ -212,6 +214,19 @@ def read_clock_probe(device: int = 0, clear: bool = True):
     check(lib.vk_read_clock_probe(device, out, 1 if clear else 0))
     cycles, ns, launches = int(out[0]), int(out[1]), int(out[2])
     return (cycles / ns * 1e3 if ns else None), launches
+
+
+TRACE_FIELDS = ("cta0_entry", "prologue_done", "first_tma", "first_stage_full", "last_mma_commit",
+                "first_acc_ready", "last_store", "cta0_exit", "min_entry", "max_entry", "min_exit", "max_exit")
+
+
+def read_trace(device: int = 0) -> dict:
+    """Timeline of the last traced launch, ns relative to the earliest CTA entry (and re-arm)."""
+    out = (ctypes.c_uint64 * 16)()
+    check(lib.vk_read_trace(device, out))
+    v = [int(x) for x in out]
+    t0 = v[8]
+    return {name: (v[i] - t0) / 1e3 for i, name in enumerate(TRACE_FIELDS)}
 
 
 def set_wait_timeout_ns(ns: int) -> None:

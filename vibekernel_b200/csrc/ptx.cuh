@@ -34,6 +34,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns()
     return t;
 }
 
+// Launch timeline (%globaltimer ns) written when the trace option is on (see vk_read_trace):
+// [0] CTA 0 entry, [1] CTA 0 prologue done, [2] first TMA issued, [3] first stage full at the MMA,
+// [4] last MMA commit, [5] first accumulator ready at the epilogue, [6] last epilogue store issued,
+// [7] CTA 0 exit, [8] earliest CTA entry, [9] latest CTA entry, [10] earliest CTA exit,
+// [11] latest CTA exit.
+__device__ unsigned long long g_trace[16];
+
+__device__ __forceinline__ void trace_at(int trace, int slot)
+{
+    if (trace && blockIdx.x == 0) g_trace[slot] = globaltimer_ns();
+}
+
 __device__ __forceinline__ void record_error(uint32_t code, uint32_t detail)
 {
     unsigned long long v = (static_cast<unsigned long long>(code) << 32) | detail;
@@ -168,6 +180,22 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* map, 
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
         : "memory");
+}
+
+// Contiguous bulk copy global -> this CTA's shared memory (no tensor map); both addresses 16-byte
+// aligned, size a multiple of 16.  Completion bytes go to `bar` in this CTA.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory accesses before later async-proxy ones.
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ------------------------------------------------------------------------------------------

@@ -56,6 +56,7 @@ struct TcParams {
     float* ws;               // split partials: [tail tile][slice][CTA rank][128 rows x BN] fp32
     int* counters;           // arrival counters: [tail tile][CTA rank][4 epilogue warps]
     int clock_probe;         // 1: CTA 0 accumulates (cycles, ns, launches) into g_clock_probe
+    int trace;               // 1: record the launch timeline into g_trace
 };
 
 struct Unit {
@@ -92,7 +93,10 @@ struct TcCfg {
     static constexpr int kBBoxes = kBNCta / 64;  // 64-column TMA boxes of B per stage
     static constexpr int kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                    : (2 * BN <= 256) ? 256 : 512;
-    static constexpr int kNumBars = 2 * STAGES + 4;
+    static constexpr int kNumBars = 2 * STAGES + 4 + 4;  // + one reduction barrier per epilogue warp
+    // The tail-split reduction stages other slices' partials in the (idle) pipeline buffers:
+    // 48 KB per epilogue warp.
+    static constexpr int kRedFloatsPerWarp = 12288;
     static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kNumBars * 8 + 16;
     static constexpr int kThreads = 192;
     static_assert(CG == 1 || CG == 2, "cta group");
@@ -100,6 +104,7 @@ struct TcCfg {
     static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "UMMA N");
     static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
     static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+    static_assert(STAGES * kStageBytes >= 4 * kRedFloatsPerWarp * 4, "reduction staging fits the stage area");
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group, int& tm, int& tn)
@@ -202,9 +207,16 @@ __global__ void __launch_bounds__(192, 1)
     auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    auto red_bar = [&](int q) { return bar0 + 8u * (2 * STAGES + 4 + q); };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    if (p.trace && threadIdx.x == 0) {
+        const unsigned long long t = globaltimer_ns();
+        if (blockIdx.x == 0) g_trace[0] = t;
+        atomicMin(&g_trace[8], t);
+        atomicMax(&g_trace[9], t);
+    }
     const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
     const int cluster_id = blockIdx.x / CG;
     const int num_clusters = gridDim.x / CG;
@@ -220,6 +232,7 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(tfull_bar(a), 1);
             mbar_init(tempty_bar(a), CG * 4);
         }
+        for (int q = 0; q < 4; ++q) mbar_init(red_bar(q), 1);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -231,6 +244,7 @@ __global__ void __launch_bounds__(192, 1)
     if constexpr (CG == 2) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    if (threadIdx.x == 0) trace_at(p.trace, 1);
     uint64_t probe_t0 = 0, probe_c0 = 0;
     if (p.clock_probe && blockIdx.x == 0 && threadIdx.x == 0) {
         probe_t0 = globaltimer_ns();
@@ -243,6 +257,7 @@ __global__ void __launch_bounds__(192, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            trace_at(p.trace, 2);
             for (int u = cluster_id; ok && u < p.units; u += num_clusters) {
                 const Unit w = unit_info(p, u);
                 int tm, tn;
@@ -313,6 +328,7 @@ __global__ void __launch_bounds__(192, 1)
                         ok = false;
                         break;
                     }
+                    if (it == 0 && kb == w.kb0) trace_at(p.trace, 3);
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
                     const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
@@ -334,6 +350,7 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t tb = tfull_bar(acc);
                 umma_commit<CG>(tb);
                 if constexpr (CG == 2) umma_commit<CG>(mapa_shared(tb, 1));
+                trace_at(p.trace, 4);
             }
         }
     } else {
@@ -345,6 +362,7 @@ __global__ void __launch_bounds__(192, 1)
             const int acc = it & 1;
             const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
             if (!mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, kErrWaitEpilogue, acc)) break;
+            if (it == 0 && warp == 2 && lane == 0) trace_at(p.trace, 5);
             tc_fence_after();
             int tm, tn;
             tile_coords(w.tile, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
@@ -388,58 +406,84 @@ __global__ void __launch_bounds__(192, 1)
                 old = __shfl_sync(0xffffffffu, old, 0);
                 if (old == p.split - 1) {
                     __threadfence();
+                    // Columns per round so that the other (split - 1) slices' partials of this warp's
+                    // 32 rows fit its 48 KB of staging: (split - 1) * cr <= 384.
+                    int cr = BN;
+                    while ((p.split - 1) * cr > Cfg::kRedFloatsPerWarp / 32) cr >>= 1;
+                    float* red = reinterpret_cast<float*>(smem) + q * Cfg::kRedFloatsPerWarp;
+                    uint32_t rphase = 0;
 #pragma unroll 1
-                    for (int c = 0; c < BN; c += 32) {
-                        if (col0 + c >= p.N) break;
-                        uint32_t r[32];
-                        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
-                        tmem_ld_wait();
-                        float own[32];
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if constexpr (ACC_F32)
-                                own[i] = __uint_as_float(r[i]);
-                            else
-                                own[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(r[i])));
-                        }
-                        // f = ((p_0 + p_1) + p_2) + ... in slice order, p_own taken from TMEM
-                        float f[32];
-#pragma unroll 1
-                        for (int s2 = 0; s2 < p.split; ++s2) {
-                            float4 v[8];
-                            if (s2 == w.slice) {
-#pragma unroll
-                                for (int j = 0; j < 8; ++j)
-                                    v[j] = make_float4(own[4 * j], own[4 * j + 1], own[4 * j + 2], own[4 * j + 3]);
-                            } else {
-                                const float4* src = reinterpret_cast<const float4*>(
-                                    p.ws + (static_cast<size_t>(ti * p.split + s2) * CG + rank) * kRegion + warp_off +
-                                    c * 32);
-#pragma unroll
-                                for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + j * 32 + lane);
-                            }
-                            if (s2 == 0) {
-#pragma unroll
-                                for (int j = 0; j < 8; ++j) {
-                                    f[4 * j] = v[j].x;
-                                    f[4 * j + 1] = v[j].y;
-                                    f[4 * j + 2] = v[j].z;
-                                    f[4 * j + 3] = v[j].w;
-                                }
-                            } else {
-#pragma unroll
-                                for (int j = 0; j < 8; ++j) {
-                                    f[4 * j] += v[j].x;
-                                    f[4 * j + 1] += v[j].y;
-                                    f[4 * j + 2] += v[j].z;
-                                    f[4 * j + 3] += v[j].w;
-                                }
+                    for (int c0 = 0; c0 < BN && col0 + c0 < p.N; c0 += cr) {
+                        if (lane == 0) {
+                            fence_proxy_async_smem();  // earlier reads of `red` precede the refill
+                            mbar_arrive_expect_tx(red_bar(q), static_cast<uint32_t>((p.split - 1) * cr * 32 * 4));
+                            int j = 0;
+                            for (int s2 = 0; s2 < p.split; ++s2) {
+                                if (s2 == w.slice) continue;
+                                const float* src = p.ws + (static_cast<size_t>(ti * p.split + s2) * CG + rank) * kRegion +
+                                                   warp_off + static_cast<size_t>(c0) * 32;
+                                bulk_load(smem_u32(red + j * cr * 32), src, static_cast<uint32_t>(cr * 32 * 4), red_bar(q));
+                                ++j;
                             }
                         }
-                        uint32_t rr[32];
+                        if (!mbar_wait(red_bar(q), rphase, p.timeout_ns, kErrWaitEpilogue, 200 + q)) break;
+                        rphase ^= 1u;
+#pragma unroll 1
+                        for (int c = c0; c < c0 + cr; c += 32) {
+                            if (col0 + c >= p.N) break;
+                            uint32_t r[32];
+                            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
+                            tmem_ld_wait();
+                            // f = ((p_0 + p_1) + p_2) + ... in slice order, p_own taken from TMEM
+                            float f[32];
+                            int j = 0;
+#pragma unroll 1
+                            for (int s2 = 0; s2 < p.split; ++s2) {
+                                float4 v[8];
+                                if (s2 == w.slice) {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(f[i]);
-                        store_chunk<true>(p, row, col0 + c, rr);
+                                    for (int jj = 0; jj < 8; ++jj) {
+                                        if constexpr (ACC_F32) {
+                                            v[jj] = make_float4(__uint_as_float(r[4 * jj]), __uint_as_float(r[4 * jj + 1]),
+                                                                __uint_as_float(r[4 * jj + 2]), __uint_as_float(r[4 * jj + 3]));
+                                        } else {
+                                            v[jj] = make_float4(
+                                                __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * jj]))),
+                                                __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * jj + 1]))),
+                                                __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * jj + 2]))),
+                                                __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * jj + 3]))));
+                                        }
+                                    }
+                                } else {
+                                    const float4* src = reinterpret_cast<const float4*>(red + j * cr * 32 + (c - c0) * 32);
+#pragma unroll
+                                    for (int jj = 0; jj < 8; ++jj) v[jj] = src[jj * 32 + lane];
+                                    ++j;
+                                }
+                                if (s2 == 0) {
+#pragma unroll
+                                    for (int jj = 0; jj < 8; ++jj) {
+                                        f[4 * jj] = v[jj].x;
+                                        f[4 * jj + 1] = v[jj].y;
+                                        f[4 * jj + 2] = v[jj].z;
+                                        f[4 * jj + 3] = v[jj].w;
+                                    }
+                                } else {
+#pragma unroll
+                                    for (int jj = 0; jj < 8; ++jj) {
+                                        f[4 * jj] += v[jj].x;
+                                        f[4 * jj + 1] += v[jj].y;
+                                        f[4 * jj + 2] += v[jj].z;
+                                        f[4 * jj + 3] += v[jj].w;
+                                    }
+                                }
+                            }
+                            uint32_t rr[32];
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(f[i]);
+                            store_chunk<true>(p, row, col0 + c, rr);
+                        }
+                        __syncwarp();
                     }
                     if (lane == 0) *ctr = 0;  // every slice has arrived: ready for the next launch
                 }
@@ -454,6 +498,7 @@ __global__ void __launch_bounds__(192, 1)
             }
             tc_fence_before();
             __syncwarp();
+            if (warp == 2 && lane == 0) trace_at(p.trace, 6);
             if (lane == 0) {
                 if constexpr (CG == 1)
                     mbar_arrive(tempty_bar(acc));
@@ -476,6 +521,12 @@ __global__ void __launch_bounds__(192, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc<CG>(tmem_base, Cfg::kTmemCols);
+    }
+    if (p.trace && threadIdx.x == 0) {
+        const unsigned long long t = globaltimer_ns();
+        if (blockIdx.x == 0) g_trace[7] = t;
+        atomicMin(&g_trace[10], t);
+        atomicMax(&g_trace[11], t);
     }
 #endif
 }

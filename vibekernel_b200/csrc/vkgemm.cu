@@ -93,6 +93,7 @@ static std::atomic<int> g_tail_split{1};
 static std::atomic<int> g_raster_group{8};
 static std::atomic<int> g_stages_2sm256{6};
 static std::atomic<int> g_clock_probe_on{0};
+static std::atomic<int> g_trace_on{0};
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -218,6 +219,7 @@ struct Schedule {
 };
 
 static constexpr int kMinSliceKb = 4;
+static constexpr int kMaxSplit = 8;
 
 static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool allow_split)
 {
@@ -231,6 +233,7 @@ static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool a
         if (rem > 0) {
             long long s = max_units / rem;
             if (s > num_kb / kMinSliceKb) s = num_kb / kMinSliceKb;
+            if (s > kMaxSplit) s = kMaxSplit;
             if (s >= 2) {
                 sc.full_units = static_cast<int>(full_waves * max_units);
                 sc.split = static_cast<int>(s);
@@ -307,6 +310,7 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb)
     p.vec_ok = (c_vec && c32_vec) ? 1 : 0;
     p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
     p.clock_probe = g_clock_probe_on.load(std::memory_order_relaxed);
+    p.trace = g_trace_on.load(std::memory_order_relaxed);
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
     const Schedule sc = plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0);
@@ -589,6 +593,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
         g_stages_2sm256.store(static_cast<int>(value));
         return VK_OK;
     }
+    if (strcmp(name, "trace") == 0) {
+        g_trace_on.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
     if (strcmp(name, "clock_probe") == 0) {
         g_clock_probe_on.store(value != 0 ? 1 : 0);
         return VK_OK;
@@ -648,6 +656,27 @@ extern "C" int vk_read_clock_probe(int device, uint64_t* out3, int clear)
     out3[0] = v[0];
     out3[1] = v[1];
     out3[2] = v[2];
+    return VK_OK;
+}
+
+extern "C" int vk_read_trace(int device, uint64_t* out16)
+{
+    if (out16 == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "out16 is NULL");
+    int prev = 0;
+    VK_CUDA_TRY(cudaGetDevice(&prev));
+    VK_CUDA_TRY(cudaSetDevice(device));
+    unsigned long long v[16];
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(v, g_trace, sizeof(v));
+    if (e == cudaSuccess) {
+        // re-arm: min slots start high, everything else at zero
+        unsigned long long z[16] = {0};
+        z[8] = z[10] = ~0ull;
+        e = cudaMemcpyToSymbol(g_trace, z, sizeof(z));
+    }
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "vk_read_trace");
+    for (int i = 0; i < 16; ++i) out16[i] = v[i];
     return VK_OK;
 }
 
