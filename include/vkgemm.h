@@ -81,6 +81,21 @@ typedef struct vk_gemm_args {
  * The general entry point.  Asynchronous; returns before the kernel finishes. */
 int vk_gemm(const vk_gemm_args* args);
 
+/* No counterpart in the reference.  Same contract as vk_gemm for the fp16 tensor-core kernels
+ * (algo AUTO, TC_2SM or TC_1SM; 16-byte aligned A/B with lda, ldb multiples of 8), for callers
+ * that cannot allocate device memory: code running during CUDA graph capture, applications whose
+ * device memory belongs to a custom pool or framework allocator that forbids side allocations,
+ * and hosts that budget every byte up front.  It calls no cudaMalloc/cudaFree: the scratch that
+ * vk_gemm would cudaMalloc once (fp32 partials of the k-sliced last wave, plus arrival counters)
+ * lives in a file-scope device array of 16 KiB + 20 MiB that every GPU loading the library holds
+ * until exit.  Enough for any problem on B200 (148 SMs); a plan needing more is rejected with
+ * VK_ERR_UNSUPPORTED and a message giving both sizes.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress, with that device current): make that first call
+ * before any stream capture.  Every call shares the one array and zeroes its counters on the
+ * given stream first, so calls that overlap on the GPU (other streams, other threads) race: order
+ * them on one stream.  The caller still passes A, B and C.  Asynchronous like vk_gemm. */
+int vk_gemm_noalloc(const vk_gemm_args* args);
+
 /* Replaces: template<> matmul<float16_t, V>(m, n, k, A, B, C), matmul.hpp:16-19 with
  * DType = float16_t (system.hpp:25).  `version` selects the kernel exactly as the
  * `--ver N` file does in the reference build (CMakeLists.txt:31-33):

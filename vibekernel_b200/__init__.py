@@ -38,7 +38,7 @@ _ACCS = {"f32": ACC_F32, "f16": ACC_F16}
 EXPORTED = (
     "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
-    "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace",
+    "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
 )
 
 
@@ -77,6 +77,8 @@ def _load() -> ctypes.CDLL:
     lib = ctypes.CDLL(LIB_PATH)
     lib.vk_gemm.argtypes = [ctypes.POINTER(GemmArgs)]
     lib.vk_gemm.restype = ctypes.c_int
+    lib.vk_gemm_noalloc.argtypes = [ctypes.POINTER(GemmArgs)]
+    lib.vk_gemm_noalloc.restype = ctypes.c_int
     sz = ctypes.c_size_t
     lib.vk_matmul_f16.argtypes = [ctypes.c_int, sz, sz, sz, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.vk_matmul_f16.restype = ctypes.c_int

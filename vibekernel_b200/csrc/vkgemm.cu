@@ -73,8 +73,19 @@ struct KernelSlot {
     int max_clusters = 0;  // co-resident clusters (CG=2) or CTAs (CG=1) at this smem size
 };
 
+// Fixed scratch for vk_gemm_noalloc: the tail-split partials and arrival counters of one call,
+// passed instead of the library's cudaMalloc'd workspace.
+struct FixedScratch {
+    float* ws;
+    int* counters;
+    size_t ws_bytes, ctr_bytes;
+};
+
 struct DeviceState {
     std::atomic<bool> ready{false};
+    // Device address of this file's static no-allocation scratch array, looked up once per device
+    // by the first vk_gemm_noalloc call made with the device current.
+    std::atomic<void*> noalloc_scratch{nullptr};
     int sm_count = 0;
     KernelSlot kernels[kMaxKernels];
     int num_kernels = 0;
@@ -280,7 +291,7 @@ struct Problem {
 };
 
 template <int CG, int BN, int STAGES, bool ACC_F32>
-static int launch_tc(DeviceState& st, int dev, const Problem& pb)
+static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScratch* fixed = nullptr)
 {
     using Cfg = TcCfg<CG, BN, STAGES, ACC_F32>;
     auto fn = tc_gemm_kernel<CG, BN, STAGES, ACC_F32>;
@@ -319,7 +330,21 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb)
     p.split = sc.split;
     p.ws = nullptr;
     p.counters = nullptr;
-    if (sc.split > 1) {
+    if (sc.split > 1 && fixed != nullptr) {
+        // Caller-provided scratch: never allocate; refuse a plan that does not fit, and zero the
+        // arrival counters this launch will use (the array keeps the previous call's contents).
+        const size_t slots = static_cast<size_t>(sc.units - sc.full_units) * CG;
+        const size_t ws_need = slots * Cfg::kBM * BN * sizeof(float);
+        const size_t ctr_need = static_cast<size_t>(sc.units - sc.full_units) / sc.split * CG * 4 * sizeof(int);
+        if (ws_need > fixed->ws_bytes || ctr_need > fixed->ctr_bytes)
+            return set_error(VK_ERR_UNSUPPORTED,
+                             "vk_gemm_noalloc: this problem needs %zu bytes of tail-split scratch and %zu bytes "
+                             "of counters; the no-allocation array holds %zu and %zu",
+                             ws_need, ctr_need, fixed->ws_bytes, fixed->ctr_bytes);
+        VK_CUDA_TRY(cudaMemsetAsync(fixed->counters, 0, ctr_need, pb.stream));
+        p.ws = fixed->ws;
+        p.counters = fixed->counters;
+    } else if (sc.split > 1) {
         rc = ensure_workspace(st, dev);
         if (rc != VK_OK) return rc;
         p.ws = st.ws;
@@ -518,6 +543,106 @@ int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc
     return f32 ? launch_tc<1, 128, 6, true>(*st, dev, pb) : launch_tc<1, 128, 6, false>(*st, dev, pb);
 }
 }  // namespace vk
+
+// ------------------------------------------------------------------------------------------
+// No-allocation entry point.  Some callers cannot call cudaMalloc at all: code running while a
+// CUDA graph is being captured, applications whose memory is owned by a custom pool or a
+// framework allocator that forbids side allocations, and hosts that budget every byte of device
+// memory up front.  vk_gemm_noalloc runs the fp16 tensor-core kernel with its tail-split scratch
+// taken from the fixed array below instead of the library's lazily cudaMalloc'd workspace.
+// ------------------------------------------------------------------------------------------
+namespace vk {
+// 16 KiB of arrival counters followed by 20 MiB of fp32 partials: one 128 x 256 fp32 slot per
+// persistent CTA on a GPU with up to 160 SMs (B200 has 148), so every problem fits on B200.
+// Every GPU that loads this library holds the array until the process exits.
+constexpr size_t kNoAllocCounterBytes = 16384;
+constexpr size_t kNoAllocPartialBytes = 20u * 1024u * 1024u;
+constexpr size_t kNoAllocScratchBytes = kNoAllocCounterBytes + kNoAllocPartialBytes;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Looks up (once per device, with that device current) the device address of the array: the
+// host-side symbol is only a stand-in and must never be passed to a kernel.
+static int noalloc_scratch(DeviceState& st, FixedScratch* out)
+{
+    void* ptr = st.noalloc_scratch.load(std::memory_order_acquire);
+    if (ptr == nullptr) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        ptr = st.noalloc_scratch.load(std::memory_order_acquire);
+        if (ptr == nullptr) {
+            cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+            st.noalloc_scratch.store(ptr, std::memory_order_release);
+        }
+    }
+    unsigned char* base = static_cast<unsigned char*>(ptr);
+    out->counters = reinterpret_cast<int*>(base);
+    out->ctr_bytes = kNoAllocCounterBytes;
+    out->ws = reinterpret_cast<float*>(base + kNoAllocCounterBytes);
+    out->ws_bytes = kNoAllocPartialBytes;
+    return VK_OK;
+}
+}  // namespace vk
+
+extern "C" int vk_gemm_noalloc(const vk_gemm_args* a)
+{
+    if (a == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_noalloc: args is NULL");
+    if (a->m < 0 || a->n < 0 || a->k < 0)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_noalloc: negative size");
+    const int64_t kMaxDim = (1LL << 31) - 1;
+    if (a->m > kMaxDim || a->n > kMaxDim || a->k > kMaxDim)
+        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm_noalloc: dimensions above 2^31-1 are not supported");
+    if (a->dtype != VK_DTYPE_F16)
+        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm_noalloc: fp16 tensor-core GEMM only");
+    if (a->acc != VK_ACC_F32 && a->acc != VK_ACC_F16)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_noalloc: unknown acc %d", a->acc);
+    if (a->algo != VK_ALGO_AUTO && a->algo != VK_ALGO_TC_2SM && a->algo != VK_ALGO_TC_1SM)
+        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm_noalloc: tensor-core kernels only (AUTO, TC_2SM, TC_1SM)");
+    if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_noalloc: tile_n must be 0, 128 or 256");
+    Problem pb;
+    pb.A = a->A;
+    pb.B = a->B;
+    pb.C = a->C;
+    pb.C32 = a->C_f32;
+    pb.m = a->m;
+    pb.n = a->n;
+    pb.k = a->k;
+    pb.lda = a->lda ? a->lda : a->k;
+    pb.ldb = a->ldb ? a->ldb : a->n;
+    pb.ldc = a->ldc ? a->ldc : a->n;
+    pb.stream = static_cast<cudaStream_t>(a->stream);
+    pb.tile_n = a->tile_n;
+    if (pb.lda < pb.k || pb.ldb < pb.n || pb.ldc < pb.n)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_noalloc: leading dimension smaller than the row length");
+
+    int dev = 0;
+    DeviceState* st = nullptr;
+    int rc = current_device(&dev, &st);
+    if (rc != VK_OK) return rc;
+    if (pb.m == 0 || pb.n == 0) return VK_OK;
+    if (pb.C == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_noalloc: C is NULL");
+    if (pb.k == 0) return launch_zero<__half>(*st, pb);
+    if (pb.A == nullptr || pb.B == nullptr)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_noalloc: A or B is NULL");
+    if (!(tma_ok_f16(pb.A, pb.lda) && tma_ok_f16(pb.B, pb.ldb)))
+        return set_error(VK_ERR_ALIGNMENT,
+                         "vk_gemm_noalloc: needs 16-byte aligned A/B and lda, ldb multiples of 8");
+    FixedScratch fx;
+    rc = noalloc_scratch(*st, &fx);
+    if (rc != VK_OK) return rc;
+    const bool f32 = a->acc == VK_ACC_F32;
+    const int tn = pb.tile_n ? pb.tile_n : 256;
+    if (a->algo != VK_ALGO_TC_1SM) {
+        if (tn == 256) {
+            if (g_stages_2sm256.load(std::memory_order_relaxed) == 7)
+                return f32 ? launch_tc<2, 256, 7, true>(*st, dev, pb, &fx) : launch_tc<2, 256, 7, false>(*st, dev, pb, &fx);
+            return f32 ? launch_tc<2, 256, 6, true>(*st, dev, pb, &fx) : launch_tc<2, 256, 6, false>(*st, dev, pb, &fx);
+        }
+        return f32 ? launch_tc<2, 128, 8, true>(*st, dev, pb, &fx) : launch_tc<2, 128, 8, false>(*st, dev, pb, &fx);
+    }
+    if (tn == 256) return f32 ? launch_tc<1, 256, 4, true>(*st, dev, pb, &fx) : launch_tc<1, 256, 4, false>(*st, dev, pb, &fx);
+    return f32 ? launch_tc<1, 128, 6, true>(*st, dev, pb, &fx) : launch_tc<1, 128, 6, false>(*st, dev, pb, &fx);
+}
 
 extern "C" int vk_matmul_f16(int version, size_t m, size_t n, size_t k, const void* A, const void* B, void* C)
 {
