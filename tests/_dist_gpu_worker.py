@@ -1,0 +1,43 @@
+"""torchrun worker for tests/test_sharded_gpu.py: one process per GPU, NCCL all-gather of C."""
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import vibekernel_b200 as vk  # noqa: E402
+from oracle import v0  # noqa: E402
+from vibekernel_b200 import dist_gemm  # noqa: E402
+
+
+def main():
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=60))
+    ok = True
+    for m in (2048, 2001):
+        A, B = v0.make_inputs(m, 1536, 768, 4)
+        off = vk.row_blocks(m, world)
+        C = torch.full((m, 1536), float("nan"), dtype=torch.float16, device=dev)
+        dist_gemm.sharded_matmul(torch.from_numpy(A[off[rank]:off[rank + 1]]).to(dev), torch.from_numpy(B).to(dev),
+                                 C, off, rank, lambda a, b, out: vk.gemm(a, b, out))
+        torch.cuda.synchronize(dev)
+        g16, _ = v0.v0_f16(A, B)
+        c = C.cpu().numpy()
+        ok = ok and not np.isnan(c.astype(np.float32)).any() and v0.max_elem_rel(c, g16) <= 2e-3
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    dist.destroy_process_group()
+    if rank == 0:
+        print("rank0 ok" if flag.item() == 1 else "rank0 FAIL", flush=True)
+    sys.exit(0 if flag.item() == 1 else 1)
+
+
+if __name__ == "__main__":
+    main()

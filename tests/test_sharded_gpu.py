@@ -1,0 +1,85 @@
+"""GPU: the row-block sharding layer against the oracle.
+
+* vk_gemm_sharded (single process, all visible GPUs, NCCL all-gather of C) -- needs >= 2 GPUs
+  for the collective; with one GPU the ngpu = 1 path (no exchange) is still exercised.
+* one process per GPU (torchrun): vibekernel_b200.dist_gemm.sharded_matmul with the CUDA kernel
+  and torch.distributed NCCL all-gather, run by tests/_dist_gpu_worker.py.
+"""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle import v0  # noqa: E402
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def vk():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    import vibekernel_b200 as vkm
+    return vkm
+
+
+def _sharded(vk, ngpu, m, n, k, allgather):
+    A, B = v0.make_inputs(m, n, k, 4)
+    off = vk.row_blocks(m, ngpu)
+    A_parts = [torch.from_numpy(A[off[r]:off[r + 1]]).cuda(r) for r in range(ngpu)]
+    B_parts = [torch.from_numpy(B).cuda(r) for r in range(ngpu)]
+    C_parts = [torch.full((m, n), float("nan"), dtype=torch.float16, device=f"cuda:{r}") for r in range(ngpu)]
+    t_compute, t_gather = vk.gemm_sharded(A_parts, B_parts, C_parts, m, n, k, allgather=allgather)
+    g16, g32 = v0.v0_f16(A, B)
+    return C_parts, off, g16, g32, t_compute, t_gather
+
+
+def test_sharded_single_gpu_no_exchange(vk):
+    C_parts, off, g16, g32, tc, tg = _sharded(vk, 1, 1000, 768, 512, allgather=False)
+    c = C_parts[0].cpu().numpy()
+    assert v0.max_elem_rel(c, g16) <= 2e-3
+    assert tc > 0 and tg == 0
+
+
+@pytest.mark.parametrize("m", [4096, 4001])  # even split (ncclAllGather) / uneven (broadcasts)
+def test_sharded_multi_gpu_allgather(vk, m):
+    ngpu = torch.cuda.device_count()
+    if ngpu < 2:
+        pytest.skip("needs >= 2 GPUs")
+    C_parts, off, g16, g32, tc, tg = _sharded(vk, ngpu, m, 2048, 1024, allgather=True)
+    for r in range(ngpu):
+        c = C_parts[r].cpu().numpy()
+        assert not np.isnan(c.astype(np.float32)).any(), f"GPU {r} missing rows after the all-gather"
+        assert v0.max_elem_rel(c, g16) <= 2e-3
+    assert tg > 0
+
+
+def test_sharded_multi_gpu_local_blocks_only(vk):
+    ngpu = torch.cuda.device_count()
+    if ngpu < 2:
+        pytest.skip("needs >= 2 GPUs")
+    m = 2048
+    C_parts, off, g16, g32, tc, tg = _sharded(vk, ngpu, m, 1024, 1024, allgather=False)
+    for r in range(ngpu):
+        c = C_parts[r].cpu().numpy()
+        blk = c[off[r]:off[r + 1]]
+        assert v0.max_elem_rel(blk, g16[off[r]:off[r + 1]]) <= 2e-3
+        outside = np.delete(c, np.s_[off[r]:off[r + 1]], axis=0)
+        assert np.isnan(outside.astype(np.float32)).all(), "a GPU wrote outside its row block"
+
+
+def test_torchrun_two_ranks(vk):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs >= 2 GPUs")
+    env = dict(os.environ, PYTHONPATH=ROOT)
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29731",
+           os.path.join(ROOT, "tests", "_dist_gpu_worker.py")]
+    res = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
+    assert "rank0 ok" in res.stdout

@@ -151,7 +151,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
 }
 
 // ------------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
+// TMA (cp.async.bulk.tensor): every load fills only the issuing CTA's own shared memory.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void prefetch_tmap(const void* map)
 {

@@ -1,7 +1,7 @@
 // Multi-GPU row-block sharding layer (vk_gemm_sharded) for single-process, multi-device callers
 // such as the task-1 C++ driver.  The reference is single-GPU (README.md:161) and has no NCCL
 // call anywhere; this layer is new.  GPU r computes C[off_r : off_r + rows_r, :] from its own A
-// slice and a full copy of B with the same tensor-core kernel as one GPU (no TMA multicast), on
+// slice and a full copy of B with the same tensor-core kernel as one GPU (local loads only), on
 // its own stream; the optional exchange is one NCCL all-gather of the C row blocks over NVLink
 // (in place, since C is row-major and the blocks are contiguous), or one broadcast per block
 // when the row split is uneven.  Processes-per-GPU callers (torchrun) shard in Python instead and

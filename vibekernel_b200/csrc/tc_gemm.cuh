@@ -19,7 +19,7 @@
 // per stage; the leader issues 256 x BN x 16 MMAs that read both CTAs' shared memory and write
 // both CTAs' TMEM.  Both CTAs' TMA loads signal the leader's "full" barrier (.cta_group::2
 // completion), and the leader's commits arrive on both CTAs' "empty" and "tmem full" barriers.
-// No TMA multicast is used anywhere, so the same binary serves 1-GPU and multi-GPU runs.
+// Every CTA loads only its own operand tiles, so the same binary serves 1-GPU and multi-GPU runs.
 //
 // Ragged shapes: TMA zero-fills out-of-range rows/columns of A and B (M, N and the K tail);
 // the epilogue predicates stores on row < M and col < N.
