@@ -242,8 +242,33 @@ def test_seven_stage_pair_kernel(vk):
     _check_f32acc(c16, c32, A, B)
 
 
+PIPELINE_OPTIONS = [{"bk_2sm256": 128}, {"fwd_empty": 1}, {"bk_2sm256": 128, "fwd_empty": 1}]
+_DEFAULTS = {"bk_2sm256": 64, "fwd_empty": 0}
+
+
+@pytest.mark.parametrize("opts", PIPELINE_OPTIONS, ids=["bk128", "relay", "bk128+relay"])
+@pytest.mark.parametrize("shape", [(1024, 1024, 1024), (4096, 4096, 4096), (4000, 5120, 3000), (200, 136, 72),
+                                   (256, 256, 4096)])
+@pytest.mark.parametrize("acc", ["f32", "f16"])
+def test_pipeline_options(vk, opts, shape, acc):
+    m, n, k = shape
+    A, B = v0.make_inputs(m, n, k, 54, lo=-0.5, hi=0.5)
+    try:
+        for name, val in opts.items():
+            vk.set_option(name, val)
+        c16, c32 = _run16(vk, A, B, algo="tc2", tile_n=256, acc=acc)
+    finally:
+        for name in opts:
+            vk.set_option(name, _DEFAULTS[name])
+    g16, g32 = v0.v0_f16(A, B)
+    if acc == "f32":
+        _check_f32acc(c16, c32, A, B)
+    else:
+        assert v0.rel_frobenius(c16.astype(np.float32), g32) <= FROB_F16ACC
+
+
 def test_options_reject_bad_values(vk):
-    for name, val in [("raster_group", 0), ("stages_2sm256", 5), ("nope", 1)]:
+    for name, val in [("raster_group", 0), ("stages_2sm256", 5), ("bk_2sm256", 96), ("nope", 1)]:
         with pytest.raises(vk.VkError):
             vk.set_option(name, val)
 

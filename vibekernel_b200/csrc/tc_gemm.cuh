@@ -57,6 +57,8 @@ struct TcParams {
     int* counters;           // arrival counters: [tail tile][CTA rank][4 epilogue warps]
     int clock_probe;         // 1: CTA 0 accumulates (cycles, ns, launches) into g_clock_probe
     int trace;               // 1: record the launch timeline into g_trace
+    int fwd_empty;           // pair mode: the MMA commits stage releases to the leader only and the
+                             // leader's producer relays each release to the peer CTA
 };
 
 struct Unit {
@@ -82,15 +84,17 @@ __device__ __forceinline__ Unit unit_info(const TcParams& p, int u)
     return w;
 }
 
-template <int CG, int BN, int STAGES, bool ACC_F32>
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
 struct TcCfg {
     static constexpr int kBM = 128;              // rows per CTA (TMEM lanes)
-    static constexpr int kBK = 64;               // k per stage = one 128-byte swizzle span of fp16
+    static constexpr int kBK = 64 * KA;          // k per stage: KA 128-byte swizzle spans of fp16
     static constexpr int kBNCta = BN / CG;       // B columns held per CTA
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = kBNCta * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kBBoxes = kBNCta / 64;  // 64-column TMA boxes of B per stage
+    static constexpr int kABox = kBM * 64 * 2;   // bytes of one 64-wide k-span of A (128 rows)
+    static constexpr int kBBox = 64 * kBK * 2;   // bytes of one 64-column box of B (kBK rows)
     static constexpr int kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                    : (2 * BN <= 256) ? 256 : 512;
     static constexpr int kNumBars = 2 * STAGES + 4 + 4;  // + one reduction barrier per epilogue warp
@@ -100,6 +104,7 @@ struct TcCfg {
     static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kNumBars * 8 + 16;
     static constexpr int kThreads = 192;
     static_assert(CG == 1 || CG == 2, "cta group");
+    static_assert(KA == 1 || KA == 2, "k spans per stage");
     static_assert(kBNCta % 64 == 0, "each CTA holds whole 64-column swizzle atoms of B");
     static_assert(BN % 16 == 0 && BN >= 64 && BN <= 256, "UMMA N");
     static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
@@ -187,13 +192,13 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col,
     }
 }
 
-template <int CG, int BN, int STAGES, bool ACC_F32>
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
 __global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const TcParams p)
 {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-    using Cfg = TcCfg<CG, BN, STAGES, ACC_F32>;
+    using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32>;
     constexpr int BM = Cfg::kBM;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -257,6 +262,8 @@ __global__ void __launch_bounds__(192, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            long long nfill = 0;  // stages filled so far by this CTA
+            const bool relay = (CG == 2) && p.fwd_empty && rank == 0;
             trace_at(p.trace, 2);
             for (int u = cluster_id; ok && u < p.units; u += num_clusters) {
                 const Unit w = unit_info(p, u);
@@ -269,23 +276,29 @@ __global__ void __launch_bounds__(192, 1)
                         ok = false;
                         break;
                     }
+                    // the MMA released fill (nfill - STAGES) of this slot: pass it on to the peer
+                    if (relay && nfill >= STAGES) mbar_arrive_cluster(mapa_shared(empty_bar(stage), 1));
+                    ++nfill;
                     const uint32_t fb = full_bar(stage);
                     const uint32_t a_dst = smem_u32(sA + stage * Cfg::kABytes);
                     const uint32_t b_dst = smem_u32(sB + stage * Cfg::kBBytes);
                     const int k0 = kb * Cfg::kBK;
                     if constexpr (CG == 1) {
                         mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-                        tma_load_2d(a_dst, &tmap_a, fb, k0, m0);
+#pragma unroll
+                        for (int a = 0; a < KA; ++a) tma_load_2d(a_dst + a * Cfg::kABox, &tmap_a, fb, k0 + 64 * a, m0);
 #pragma unroll
                         for (int j = 0; j < Cfg::kBBoxes; ++j)
-                            tma_load_2d(b_dst + j * 8192, &tmap_b, fb, n0 + 64 * j, k0);
+                            tma_load_2d(b_dst + j * Cfg::kBBox, &tmap_b, fb, n0 + 64 * j, k0);
                     } else {
                         if (rank == 0) mbar_arrive_expect_tx(fb, 2 * Cfg::kStageBytes);
                         const uint32_t fb_leader = mapa_shared(fb, 0);
-                        tma_load_2d_pair(a_dst, &tmap_a, fb_leader, k0, m0);
+#pragma unroll
+                        for (int a = 0; a < KA; ++a)
+                            tma_load_2d_pair(a_dst + a * Cfg::kABox, &tmap_a, fb_leader, k0 + 64 * a, m0);
 #pragma unroll
                         for (int j = 0; j < Cfg::kBBoxes; ++j)
-                            tma_load_2d_pair(b_dst + j * 8192, &tmap_b, fb_leader, n0 + 64 * j, k0);
+                            tma_load_2d_pair(b_dst + j * Cfg::kBBox, &tmap_b, fb_leader, n0 + 64 * j, k0);
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -298,6 +311,7 @@ __global__ void __launch_bounds__(192, 1)
             if (ok) {
                 for (int i = 0; i < STAGES; ++i) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, kErrWaitTail, stage)) break;
+                    if (relay && nfill - STAGES + i >= 0) mbar_arrive_cluster(mapa_shared(empty_bar(stage), 1));
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
@@ -334,13 +348,15 @@ __global__ void __launch_bounds__(192, 1)
                     const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
 #pragma unroll
                     for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
-                        const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+                        const uint64_t a_desc = smem_desc_sw128(a_addr + (kk >> 2) * Cfg::kABox + (kk & 3) * 32, 16, 1024);
                         const uint64_t b_desc = smem_desc_sw128(b_addr + kk * 16 * 128, kBLbo, 1024);
                         umma_f16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
                     }
                     const uint32_t eb = empty_bar(stage);
                     umma_commit<CG>(eb);
-                    if constexpr (CG == 2) umma_commit<CG>(mapa_shared(eb, 1));
+                    if constexpr (CG == 2) {
+                        if (!p.fwd_empty) umma_commit<CG>(mapa_shared(eb, 1));
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;

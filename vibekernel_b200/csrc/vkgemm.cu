@@ -103,6 +103,8 @@ static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 static std::atomic<int> g_tail_split{1};
 static std::atomic<int> g_raster_group{8};
 static std::atomic<int> g_stages_2sm256{6};
+static std::atomic<int> g_bk_2sm256{64};
+static std::atomic<int> g_fwd_empty{0};
 static std::atomic<int> g_clock_probe_on{0};
 static std::atomic<int> g_trace_on{0};
 
@@ -290,11 +292,11 @@ struct Problem {
     int tile_n;
 };
 
-template <int CG, int BN, int STAGES, bool ACC_F32>
-static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScratch* fixed = nullptr)
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
+static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScratch* fixed)
 {
-    using Cfg = TcCfg<CG, BN, STAGES, ACC_F32>;
-    auto fn = tc_gemm_kernel<CG, BN, STAGES, ACC_F32>;
+    using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32>;
+    auto fn = tc_gemm_kernel<CG, BN, STAGES, KA, ACC_F32>;
     int max_units = 0;
     int rc = kernel_slot(st, fn, Cfg::kSmemBytes, Cfg::kThreads, CG, &max_units);
     if (rc != VK_OK) return rc;
@@ -322,6 +324,7 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
     p.clock_probe = g_clock_probe_on.load(std::memory_order_relaxed);
     p.trace = g_trace_on.load(std::memory_order_relaxed);
+    p.fwd_empty = g_fwd_empty.load(std::memory_order_relaxed);
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
     const Schedule sc = plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0);
@@ -366,6 +369,23 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     cfg.numAttrs = 1;
     VK_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, ta, tb, p));
     return VK_OK;
+}
+
+// One tensor-core variant per (pair or single CTA, tile N, accumulate type, pipeline shape).
+template <bool F32>
+static int launch_tc_variant(DeviceState& st, int dev, const Problem& pb, int algo, const FixedScratch* fixed)
+{
+    const int tn = pb.tile_n ? pb.tile_n : 256;
+    if (algo == VK_ALGO_TC_2SM) {
+        if (tn == 256) {
+            if (g_bk_2sm256.load(std::memory_order_relaxed) == 128) return launch_tc<2, 256, 3, 2, F32>(st, dev, pb, fixed);
+            if (g_stages_2sm256.load(std::memory_order_relaxed) == 7) return launch_tc<2, 256, 7, 1, F32>(st, dev, pb, fixed);
+            return launch_tc<2, 256, 6, 1, F32>(st, dev, pb, fixed);
+        }
+        return launch_tc<2, 128, 8, 1, F32>(st, dev, pb, fixed);
+    }
+    if (tn == 256) return launch_tc<1, 256, 4, 1, F32>(st, dev, pb, fixed);
+    return launch_tc<1, 128, 6, 1, F32>(st, dev, pb, fixed);
 }
 
 static int launch_sgemm(const Problem& pb)
@@ -529,18 +549,8 @@ int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc
         return set_error(VK_ERR_ALIGNMENT,
                          "vk_gemm: tensor-core kernels need 16-byte aligned A/B and lda, ldb multiples of 8 "
                          "(use VK_ALGO_AUTO or VK_ALGO_SIMT)");
-    const int tn = pb.tile_n ? pb.tile_n : 256;
-    const bool f32 = acc == VK_ACC_F32;
-    if (algo == VK_ALGO_TC_2SM) {
-        if (tn == 256) {
-            if (g_stages_2sm256.load(std::memory_order_relaxed) == 7)
-                return f32 ? launch_tc<2, 256, 7, true>(*st, dev, pb) : launch_tc<2, 256, 7, false>(*st, dev, pb);
-            return f32 ? launch_tc<2, 256, 6, true>(*st, dev, pb) : launch_tc<2, 256, 6, false>(*st, dev, pb);
-        }
-        return f32 ? launch_tc<2, 128, 8, true>(*st, dev, pb) : launch_tc<2, 128, 8, false>(*st, dev, pb);
-    }
-    if (tn == 256) return f32 ? launch_tc<1, 256, 4, true>(*st, dev, pb) : launch_tc<1, 256, 4, false>(*st, dev, pb);
-    return f32 ? launch_tc<1, 128, 6, true>(*st, dev, pb) : launch_tc<1, 128, 6, false>(*st, dev, pb);
+    return acc == VK_ACC_F32 ? launch_tc_variant<true>(*st, dev, pb, algo, nullptr)
+                             : launch_tc_variant<false>(*st, dev, pb, algo, nullptr);
 }
 }  // namespace vk
 
@@ -630,18 +640,9 @@ extern "C" int vk_gemm_noalloc(const vk_gemm_args* a)
     FixedScratch fx;
     rc = noalloc_scratch(*st, &fx);
     if (rc != VK_OK) return rc;
-    const bool f32 = a->acc == VK_ACC_F32;
-    const int tn = pb.tile_n ? pb.tile_n : 256;
-    if (a->algo != VK_ALGO_TC_1SM) {
-        if (tn == 256) {
-            if (g_stages_2sm256.load(std::memory_order_relaxed) == 7)
-                return f32 ? launch_tc<2, 256, 7, true>(*st, dev, pb, &fx) : launch_tc<2, 256, 7, false>(*st, dev, pb, &fx);
-            return f32 ? launch_tc<2, 256, 6, true>(*st, dev, pb, &fx) : launch_tc<2, 256, 6, false>(*st, dev, pb, &fx);
-        }
-        return f32 ? launch_tc<2, 128, 8, true>(*st, dev, pb, &fx) : launch_tc<2, 128, 8, false>(*st, dev, pb, &fx);
-    }
-    if (tn == 256) return f32 ? launch_tc<1, 256, 4, true>(*st, dev, pb, &fx) : launch_tc<1, 256, 4, false>(*st, dev, pb, &fx);
-    return f32 ? launch_tc<1, 128, 6, true>(*st, dev, pb, &fx) : launch_tc<1, 128, 6, false>(*st, dev, pb, &fx);
+    const int algo = a->algo == VK_ALGO_TC_1SM ? VK_ALGO_TC_1SM : VK_ALGO_TC_2SM;
+    return a->acc == VK_ACC_F32 ? launch_tc_variant<true>(*st, dev, pb, algo, &fx)
+                                : launch_tc_variant<false>(*st, dev, pb, algo, &fx);
 }
 
 extern "C" int vk_matmul_f16(int version, size_t m, size_t n, size_t k, const void* A, const void* B, void* C)
@@ -716,6 +717,15 @@ extern "C" int vk_set_option(const char* name, int64_t value)
     if (strcmp(name, "stages_2sm256") == 0) {
         if (value != 6 && value != 7) return set_error(VK_ERR_INVALID_ARGUMENT, "stages_2sm256 must be 6 or 7");
         g_stages_2sm256.store(static_cast<int>(value));
+        return VK_OK;
+    }
+    if (strcmp(name, "bk_2sm256") == 0) {
+        if (value != 64 && value != 128) return set_error(VK_ERR_INVALID_ARGUMENT, "bk_2sm256 must be 64 or 128");
+        g_bk_2sm256.store(static_cast<int>(value));
+        return VK_OK;
+    }
+    if (strcmp(name, "fwd_empty") == 0) {
+        g_fwd_empty.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
     if (strcmp(name, "trace") == 0) {
