@@ -153,10 +153,8 @@ int vk_set_wait_timeout_ns(uint64_t ns);
 /* Process-wide tuning knobs (no counterpart in the reference, whose versions hard-code them):
  *   "tail_split"      1 (default) = cut the tiles of a partial last wave into k-slices, 0 = off
  *   "raster_group"    tiles along M per rasterisation group of the persistent scheduler (8)
- *   "stages_2sm256"   shared-memory pipeline depth of the 256-column pair kernel (6 or 7)
- *   "bk_2sm256"       k per pipeline stage of the 256-column pair kernel: 64 (6 stages) or 128 (3)
- *   "fwd_empty"       1 = pair kernels commit each stage release to the leader CTA only and the
- *                     leader's producer relays it to the peer (one commit per stage instead of two)
+ *   "bk_2sm256"       k per pipeline stage of the 256-column pair kernel: 128 (default, 3 stages
+ *                     of 64 KB) or 64 (6 stages of 32 KB)
  *   "wait_timeout_ns" same as vk_set_wait_timeout_ns
  *   "clock_probe"     1 = the tensor-core kernels accumulate the SM cycles and nanoseconds of
  *                     their first CTA (read with vk_read_clock_probe); 0 (default) = off

@@ -232,21 +232,11 @@ def test_tail_split_matches_unsplit(vk, shape):
         assert v0.max_elem_rel(c, g32) <= ELEM
 
 
-def test_seven_stage_pair_kernel(vk):
-    A, B = v0.make_inputs(1024, 2048, 1536, 53)
-    try:
-        vk.set_option("stages_2sm256", 7)
-        c16, c32 = _run16(vk, A, B, algo="tc2", tile_n=256)
-    finally:
-        vk.set_option("stages_2sm256", 6)
-    _check_f32acc(c16, c32, A, B)
+PIPELINE_OPTIONS = [{"bk_2sm256": 64}, {"bk_2sm256": 64, "tail_split": 0}, {"tail_split": 0}]
+_DEFAULTS = {"bk_2sm256": 128, "tail_split": 1}
 
 
-PIPELINE_OPTIONS = [{"bk_2sm256": 128}, {"fwd_empty": 1}, {"bk_2sm256": 128, "fwd_empty": 1}]
-_DEFAULTS = {"bk_2sm256": 64, "fwd_empty": 0}
-
-
-@pytest.mark.parametrize("opts", PIPELINE_OPTIONS, ids=["bk128", "relay", "bk128+relay"])
+@pytest.mark.parametrize("opts", PIPELINE_OPTIONS, ids=["bk64", "bk64-nosplit", "bk128-nosplit"])
 @pytest.mark.parametrize("shape", [(1024, 1024, 1024), (4096, 4096, 4096), (4000, 5120, 3000), (200, 136, 72),
                                    (256, 256, 4096)])
 @pytest.mark.parametrize("acc", ["f32", "f16"])
@@ -268,7 +258,7 @@ def test_pipeline_options(vk, opts, shape, acc):
 
 
 def test_options_reject_bad_values(vk):
-    for name, val in [("raster_group", 0), ("stages_2sm256", 5), ("bk_2sm256", 96), ("nope", 1)]:
+    for name, val in [("raster_group", 0), ("bk_2sm256", 96), ("fwd_empty", 1), ("nope", 1)]:
         with pytest.raises(vk.VkError):
             vk.set_option(name, val)
 

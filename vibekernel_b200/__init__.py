@@ -206,7 +206,7 @@ def device_error(device: int = 0, clear: bool = True) -> int:
 
 
 def set_option(name: str, value: int) -> None:
-    """Process-wide knob: tail_split, raster_group, stages_2sm256, wait_timeout_ns."""
+    """Process-wide knob: tail_split, raster_group, bk_2sm256, clock_probe, trace, wait_timeout_ns."""
     check(lib.vk_set_option(name.encode(), int(value)))
 
 

@@ -57,8 +57,6 @@ struct TcParams {
     int* counters;           // arrival counters: [tail tile][CTA rank][4 epilogue warps]
     int clock_probe;         // 1: CTA 0 accumulates (cycles, ns, launches) into g_clock_probe
     int trace;               // 1: record the launch timeline into g_trace
-    int fwd_empty;           // pair mode: the MMA commits stage releases to the leader only and the
-                             // leader's producer relays each release to the peer CTA
 };
 
 struct Unit {
@@ -262,8 +260,6 @@ __global__ void __launch_bounds__(192, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            long long nfill = 0;  // stages filled so far by this CTA
-            const bool relay = (CG == 2) && p.fwd_empty && rank == 0;
             trace_at(p.trace, 2);
             for (int u = cluster_id; ok && u < p.units; u += num_clusters) {
                 const Unit w = unit_info(p, u);
@@ -276,9 +272,6 @@ __global__ void __launch_bounds__(192, 1)
                         ok = false;
                         break;
                     }
-                    // the MMA released fill (nfill - STAGES) of this slot: pass it on to the peer
-                    if (relay && nfill >= STAGES) mbar_arrive_cluster(mapa_shared(empty_bar(stage), 1));
-                    ++nfill;
                     const uint32_t fb = full_bar(stage);
                     const uint32_t a_dst = smem_u32(sA + stage * Cfg::kABytes);
                     const uint32_t b_dst = smem_u32(sB + stage * Cfg::kBBytes);
@@ -311,7 +304,6 @@ __global__ void __launch_bounds__(192, 1)
             if (ok) {
                 for (int i = 0; i < STAGES; ++i) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, kErrWaitTail, stage)) break;
-                    if (relay && nfill - STAGES + i >= 0) mbar_arrive_cluster(mapa_shared(empty_bar(stage), 1));
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
@@ -354,9 +346,7 @@ __global__ void __launch_bounds__(192, 1)
                     }
                     const uint32_t eb = empty_bar(stage);
                     umma_commit<CG>(eb);
-                    if constexpr (CG == 2) {
-                        if (!p.fwd_empty) umma_commit<CG>(mapa_shared(eb, 1));
-                    }
+                    if constexpr (CG == 2) umma_commit<CG>(mapa_shared(eb, 1));
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;

@@ -102,9 +102,10 @@ static DeviceState g_dev[kMaxDevices];
 static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 static std::atomic<int> g_tail_split{1};
 static std::atomic<int> g_raster_group{8};
-static std::atomic<int> g_stages_2sm256{6};
-static std::atomic<int> g_bk_2sm256{64};
-static std::atomic<int> g_fwd_empty{0};
+// k depth per pipeline stage of the 256-column pair kernel.  Every stage ends with tcgen05.commit
+// to both CTAs' "empty" barriers, and those commits measurably throttle the tensor pipe; 128-deep
+// stages (3 x 64 KB) halve them per MMA and beat 64-deep ones (6 x 32 KB) at every size measured.
+static std::atomic<int> g_bk_2sm256{128};
 static std::atomic<int> g_clock_probe_on{0};
 static std::atomic<int> g_trace_on{0};
 
@@ -324,7 +325,6 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
     p.clock_probe = g_clock_probe_on.load(std::memory_order_relaxed);
     p.trace = g_trace_on.load(std::memory_order_relaxed);
-    p.fwd_empty = g_fwd_empty.load(std::memory_order_relaxed);
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
     const Schedule sc = plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0);
@@ -379,7 +379,6 @@ static int launch_tc_variant(DeviceState& st, int dev, const Problem& pb, int al
     if (algo == VK_ALGO_TC_2SM) {
         if (tn == 256) {
             if (g_bk_2sm256.load(std::memory_order_relaxed) == 128) return launch_tc<2, 256, 3, 2, F32>(st, dev, pb, fixed);
-            if (g_stages_2sm256.load(std::memory_order_relaxed) == 7) return launch_tc<2, 256, 7, 1, F32>(st, dev, pb, fixed);
             return launch_tc<2, 256, 6, 1, F32>(st, dev, pb, fixed);
         }
         return launch_tc<2, 128, 8, 1, F32>(st, dev, pb, fixed);
@@ -714,18 +713,9 @@ extern "C" int vk_set_option(const char* name, int64_t value)
         g_raster_group.store(static_cast<int>(value));
         return VK_OK;
     }
-    if (strcmp(name, "stages_2sm256") == 0) {
-        if (value != 6 && value != 7) return set_error(VK_ERR_INVALID_ARGUMENT, "stages_2sm256 must be 6 or 7");
-        g_stages_2sm256.store(static_cast<int>(value));
-        return VK_OK;
-    }
     if (strcmp(name, "bk_2sm256") == 0) {
         if (value != 64 && value != 128) return set_error(VK_ERR_INVALID_ARGUMENT, "bk_2sm256 must be 64 or 128");
         g_bk_2sm256.store(static_cast<int>(value));
-        return VK_OK;
-    }
-    if (strcmp(name, "fwd_empty") == 0) {
-        g_fwd_empty.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
     if (strcmp(name, "trace") == 0) {
