@@ -342,6 +342,8 @@ def main():
         achieved = 2.0 * rows * n * k / (kernel_ms * 1e-3) / 1e12
         roof = {"bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": roof_unit,
                 "frac": round(achieved / peak, 4), "traffic": TRAFFIC.get(args.workload),
+                "traffic_unit": "bytes/launch",
+                "algorithmic_bytes": int((rows * k + k * n + rows * n) * (2 if dt == "f16" else 4)),
                 "peak_source": (f"MEASURED_PEAKS.json bf16_tflops (burst), of {pk_src}" if dt == "f16"
                                 else "148 SMs x 128 FP32 lanes x 2 x sampled SM clock")}
         line = {
@@ -379,9 +381,10 @@ def main():
         dist.destroy_process_group()
 
 
-# DRAM bytes (read + write) per launch from the ncu capture summarised under profiles/; None
-# until a capture exists for the workload.
-TRAFFIC = {}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernel, from
+# the ncu captures summarised in profiles/tc_gemm_pair_rubric4096.md and profiles/sgemm_ffma_4096.md;
+# None where no capture of the current kernel exists.
+TRAFFIC = {"rubric": 104911616, "sgemm": 400398592}
 
 if __name__ == "__main__":
     main()
