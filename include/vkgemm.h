@@ -96,6 +96,15 @@ int vk_gemm(const vk_gemm_args* args);
  * them on one stream.  The caller still passes A, B and C.  Asynchronous like vk_gemm. */
 int vk_gemm_noalloc(const vk_gemm_args* args);
 
+/* Replaces: the reference harness's host-side flow around one matmul call -- copy A and B to the
+ * device, call, copy C back (test_data.hpp:177-196, main.cpp:46-62) -- for callers whose A, B and C
+ * are in HOST memory.  Same fields as vk_gemm (A, B, C are host pointers; C_f32 must be NULL;
+ * `stream` is ignored).  The copies are pipelined with the computation in row blocks of
+ * `block_rows` rows (0 = automatic, about 8 blocks); device staging buffers are cached per device
+ * (freed by vk_shutdown).  Synchronous: returns when C is in host memory.  Pinned host memory
+ * gives full PCIe bandwidth.  Calls from several threads are serialised. */
+int vk_gemm_host(const vk_gemm_args* args, int32_t block_rows);
+
 /* Replaces: template<> matmul<float16_t, V>(m, n, k, A, B, C), matmul.hpp:16-19 with
  * DType = float16_t (system.hpp:25).  `version` selects the kernel exactly as the
  * `--ver N` file does in the reference build (CMakeLists.txt:31-33):

@@ -39,6 +39,7 @@ EXPORTED = (
     "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
     "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
+    "vk_gemm_host",
 )
 
 
@@ -79,6 +80,8 @@ def _load() -> ctypes.CDLL:
     lib.vk_gemm.restype = ctypes.c_int
     lib.vk_gemm_noalloc.argtypes = [ctypes.POINTER(GemmArgs)]
     lib.vk_gemm_noalloc.restype = ctypes.c_int
+    lib.vk_gemm_host.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_int32]
+    lib.vk_gemm_host.restype = ctypes.c_int
     sz = ctypes.c_size_t
     lib.vk_matmul_f16.argtypes = [ctypes.c_int, sz, sz, sz, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.vk_matmul_f16.restype = ctypes.c_int
@@ -177,6 +180,44 @@ def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile
     a.stream = _stream_handle(stream)
     with torch.cuda.device(A.device):
         check(lib.vk_gemm(ctypes.byref(a)))
+    return C
+
+
+def gemm_host(A, B, C=None, *, acc: str = "f32", algo: str = "auto", block_rows: int = 0):
+    """C = A @ B for HOST operands through ``vk_gemm_host`` (copies pipelined with the GEMM).
+
+    A, B, C: CPU torch tensors (pin them for full PCIe bandwidth) or numpy arrays, row-major with
+    unit column stride, fp16 or fp32.  Synchronous; returns C.
+    """
+    import numpy as np
+
+    def info(t):
+        if isinstance(t, np.ndarray):
+            if t.ndim != 2 or t.strides[1] != t.itemsize:
+                raise ValueError("2-D arrays with unit column stride only")
+            return t.ctypes.data, t.strides[0] // t.itemsize, t.dtype == np.float16, t.shape
+        if t.is_cuda or t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError("CPU 2-D tensors with unit column stride only")
+        import torch
+        return t.data_ptr(), t.stride(0), t.dtype == torch.float16, tuple(t.shape)
+
+    pa, lda, f16a, (m, k) = info(A)
+    pb, ldb, f16b, (k2, n) = info(B)
+    if k2 != k or f16a != f16b:
+        raise ValueError("shape or dtype mismatch")
+    if C is None:
+        C = np.empty((m, n), dtype=np.float16 if f16a else np.float32)
+    pc, ldc, f16c, shape_c = info(C)
+    if shape_c != (m, n) or f16c != f16a:
+        raise ValueError("C has the wrong shape or dtype")
+    a = GemmArgs()
+    a.A, a.B, a.C = pa, pb, pc
+    a.m, a.n, a.k = m, n, k
+    a.lda, a.ldb, a.ldc = max(lda, 1), max(ldb, 1), max(ldc, 1)
+    a.dtype = DTYPE_F16 if f16a else DTYPE_F32
+    a.acc = _ACCS[acc]
+    a.algo = _ALGOS[algo]
+    check(lib.vk_gemm_host(ctypes.byref(a), block_rows))
     return C
 
 

@@ -240,5 +240,6 @@ extern "C" int vk_shutdown(void)
     g_groups.clear();
     cudaSetDevice(prev);
     vk::release_device_state();
+    vk::release_host_pipes();
     return VK_OK;
 }

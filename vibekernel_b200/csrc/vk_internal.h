@@ -6,4 +6,6 @@ namespace vk {
 int set_error(int code, const char* fmt, ...);
 // Frees per-device scratch owned by the library (vk_shutdown).
 void release_device_state();
+// Frees the host-buffer pipeline's staging buffers and streams (vk_shutdown).
+void release_host_pipes();
 }  // namespace vk
