@@ -100,7 +100,7 @@ int vk_gemm_noalloc(const vk_gemm_args* args);
  * device, call, copy C back (test_data.hpp:177-196, main.cpp:46-62) -- for callers whose A, B and C
  * are in HOST memory.  Same fields as vk_gemm (A, B, C are host pointers; C_f32 must be NULL;
  * `stream` is ignored).  The copies are pipelined with the computation in row blocks of
- * `block_rows` rows (0 = automatic, about 8 blocks); device staging buffers are cached per device
+ * `block_rows` rows (0 = automatic, about 4 blocks); device staging buffers are cached per device
  * (freed by vk_shutdown).  Synchronous: returns when C is in host memory.  Pinned host memory
  * gives full PCIe bandwidth.  Calls from several threads are serialised. */
 int vk_gemm_host(const vk_gemm_args* args, int32_t block_rows);

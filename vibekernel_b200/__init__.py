@@ -193,7 +193,11 @@ def gemm_host(A, B, C=None, *, acc: str = "f32", algo: str = "auto", block_rows:
 
     def info(t):
         if isinstance(t, np.ndarray):
-            if t.ndim != 2 or t.strides[1] != t.itemsize:
+            if t.ndim != 2:
+                raise ValueError("2-D arrays only")
+            if t.size == 0:  # numpy reports zero strides for empty arrays
+                return t.ctypes.data, max(t.shape[1], 1), t.dtype == np.float16, t.shape
+            if t.strides[1] != t.itemsize:
                 raise ValueError("2-D arrays with unit column stride only")
             return t.ctypes.data, t.strides[0] // t.itemsize, t.dtype == np.float16, t.shape
         if t.is_cuda or t.dim() != 2 or t.stride(1) != 1:

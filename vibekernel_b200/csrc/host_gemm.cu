@@ -115,8 +115,9 @@ extern "C" int vk_gemm_host(const vk_gemm_args* a, int32_t block_rows)
     if (rc == VK_OK) rc = ensure(&hp.dC, &hp.capC, static_cast<size_t>(m) * n * es);
     if (rc != VK_OK) return rc;
 
-    // Row blocks: about 8 blocks, multiples of 256 rows (one pair tile), at least 256 rows.
-    int64_t rows = block_rows > 0 ? block_rows : ((m + 7) / 8 + 255) / 256 * 256;
+    // Row blocks: about 4 blocks (measured best at 4096^3 on B200 among 1-16 blocks), multiples of
+    // 256 rows (one pair tile), at least 256 rows.
+    int64_t rows = block_rows > 0 ? block_rows : ((m + 3) / 4 + 255) / 256 * 256;
     if (rows < 1) rows = 1;
     const int64_t nblk = (m + rows - 1) / rows;
 
