@@ -214,6 +214,29 @@ def test_repeated_launches_are_bitwise_identical(vk, shape, acc):
     assert v0.rel_frobenius(first.cpu().numpy().astype(np.float32), g32) <= max(tol, 5e-4)
 
 
+def test_split_gemms_on_concurrent_streams(vk):
+    """Two k-sliced GEMMs in flight on different streams must not share tail-split scratch."""
+    A1, B1 = v0.make_inputs(1024, 1024, 2048, 55)
+    A2, B2 = v0.make_inputs(1024, 1024, 2048, 56)
+    d = [(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()) for A, B in ((A1, B1), (A2, B2))]
+    ref = [vk.gemm(a, b).clone() for a, b in d]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [torch.empty_like(ref[0]), torch.empty_like(ref[1])]
+    bad = 0
+    for it in range(60):
+        for i in (0, 1):
+            with torch.cuda.stream(streams[i]):
+                outs[i].fill_(float("nan"))
+                vk.gemm(d[i][0], d[i][1], outs[i])
+        if it % 10 == 9:
+            torch.cuda.synchronize()
+            bad += sum(int(not torch.equal(outs[i].view(torch.int16), ref[i].view(torch.int16))) for i in (0, 1))
+    torch.cuda.synchronize()
+    assert bad == 0
+    assert vk.device_error(0) == 0
+
+
 @pytest.mark.parametrize("shape", [(1024, 1024, 1024), (4096, 4096, 4096), (4000, 5120, 3000), (300, 200, 4096),
                                    (256, 256, 4096), (512, 768, 2048), (700, 1000, 1200)])
 def test_tail_split_matches_unsplit(vk, shape):

@@ -89,11 +89,19 @@ struct DeviceState {
     int sm_count = 0;
     KernelSlot kernels[kMaxKernels];
     int num_kernels = 0;
-    // Tail-split scratch, allocated once on first need: fp32 partials for at most one unit per
-    // persistent CTA (sm_count x 128 x 256 floats, 19.4 MB on 148 SMs) and 4 arrival counters
-    // per CTA (zeroed at allocation; each reduction leaves them zero again).
-    float* ws = nullptr;
-    int* counters = nullptr;
+    // Tail-split scratch, one per stream that launched a split GEMM (launches on different streams
+    // may overlap on the GPU, so they must not share partials or counters), allocated on first
+    // need: fp32 partials for at most one unit per persistent CTA (sm_count x 128 x 256 floats,
+    // 19.4 MB on 148 SMs) and 4 arrival counters per CTA (zeroed at allocation; each reduction
+    // leaves them zero again).
+    struct StreamScratch {
+        cudaStream_t stream = nullptr;
+        float* ws = nullptr;
+        int* counters = nullptr;
+    };
+    static constexpr int kMaxStreams = 32;
+    StreamScratch scratch[kMaxStreams];
+    int num_scratch = 0;
     size_t ws_bytes = 0, ctr_bytes = 0;
 };
 
@@ -201,12 +209,22 @@ static int kernel_slot(DeviceState& st, Kernel fn, int smem, int threads, int cl
     return VK_OK;
 }
 
-// Tail-split workspace for the current device (allocated once; see DeviceState).
-static int ensure_workspace(DeviceState& st, int dev)
+// Tail-split workspace of (current device, stream), allocated on first use; see DeviceState.
+static int ensure_workspace(DeviceState& st, int dev, cudaStream_t stream, float** ws_out, int** ctr_out)
 {
-    if (st.ws != nullptr) return VK_OK;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (st.ws != nullptr) return VK_OK;
+    for (int i = 0; i < st.num_scratch; ++i) {
+        if (st.scratch[i].stream == stream) {
+            *ws_out = st.scratch[i].ws;
+            *ctr_out = st.scratch[i].counters;
+            return VK_OK;
+        }
+    }
+    if (st.num_scratch >= DeviceState::kMaxStreams)
+        return set_error(VK_ERR_UNSUPPORTED,
+                         "tail-split workspaces exist for %d streams on device %d; use fewer streams or "
+                         "vk_set_option(\"tail_split\", 0)",
+                         DeviceState::kMaxStreams, dev);
     const size_t ws_bytes = static_cast<size_t>(st.sm_count) * 128 * 256 * sizeof(float);
     const size_t ctr_bytes = static_cast<size_t>(st.sm_count) * 4 * sizeof(int);
     float* ws = nullptr;
@@ -221,8 +239,12 @@ static int ensure_workspace(DeviceState& st, int dev)
     }
     st.ctr_bytes = ctr_bytes;
     st.ws_bytes = ws_bytes;
-    st.counters = ctr;
-    st.ws = ws;
+    DeviceState::StreamScratch& s = st.scratch[st.num_scratch++];
+    s.stream = stream;
+    s.ws = ws;
+    s.counters = ctr;
+    *ws_out = ws;
+    *ctr_out = ctr;
     return VK_OK;
 }
 
@@ -348,10 +370,8 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
         p.ws = fixed->ws;
         p.counters = fixed->counters;
     } else if (sc.split > 1) {
-        rc = ensure_workspace(st, dev);
+        rc = ensure_workspace(st, dev, pb.stream, &p.ws, &p.counters);
         if (rc != VK_OK) return rc;
-        p.ws = st.ws;
-        p.counters = st.counters;
     }
     const int clusters = sc.grid_units;
 
@@ -456,12 +476,14 @@ void release_device_state()
     cudaGetDevice(&prev);
     for (int d = 0; d < kMaxDevices; ++d) {
         DeviceState& st = g_dev[d];
-        if (st.ws == nullptr) continue;
+        if (st.num_scratch == 0) continue;
         cudaSetDevice(d);
-        cudaFree(st.ws);
-        cudaFree(st.counters);
-        st.ws = nullptr;
-        st.counters = nullptr;
+        for (int i = 0; i < st.num_scratch; ++i) {
+            cudaFree(st.scratch[i].ws);
+            cudaFree(st.scratch[i].counters);
+            st.scratch[i] = DeviceState::StreamScratch();
+        }
+        st.num_scratch = 0;
         st.ws_bytes = st.ctr_bytes = 0;
     }
     cudaSetDevice(prev);
@@ -754,8 +776,12 @@ extern "C" int vk_device_error(int device, uint64_t* out_word, int clear)
         const unsigned long long z = 0;
         e = cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
         // a kernel that gave up may have left tail-split arrival counters mid-count
-        if (e == cudaSuccess && device >= 0 && device < kMaxDevices && g_dev[device].counters != nullptr)
-            e = cudaMemset(g_dev[device].counters, 0, g_dev[device].ctr_bytes);
+        if (device >= 0 && device < kMaxDevices) {
+            std::lock_guard<std::mutex> lk(g_mu);
+            DeviceState& st = g_dev[device];
+            for (int i = 0; i < st.num_scratch && e == cudaSuccess; ++i)
+                e = cudaMemset(st.scratch[i].counters, 0, st.ctr_bytes);
+        }
     }
     cudaSetDevice(prev);
     if (e != cudaSuccess) return cuda_fail(e, "vk_device_error");
