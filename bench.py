@@ -150,14 +150,19 @@ def run_reference(args, cfg):
     npdt = np.float16 if dt == "f16" else np.float32
     A, B = v0.make_inputs(m, n, k, seed, dist, lo, hi, npdt)
     kind = "reference" if v0.ref_available() else "port"
-    # size every step so that warmup + steps finish in about two minutes
+    fn = (v0.ref_v0_f16 if dt == "f16" else v0.ref_v0_f32) if v0.ref_available() else \
+        ((lambda a, b: v0.v0_f16(a, b)[0]) if dt == "f16" else v0.v0_f32)
+    # Calibrate once: every step is one v0 call on a row slice of A sized so that warm-up + steps
+    # finish in about two minutes (the full matrix when that fits).
     per_step = max(0.05, 120.0 / max(1, args.steps + args.warmup))
+    _, rows_used, _ = cpu_v0_sample(A, B, dt, per_step)
     tfl = []
-    rows_used = 0
     for i in range(args.warmup + args.steps):
-        t, rows_used, _ = cpu_v0_sample(A, B, dt, per_step if i == 0 else per_step)
+        t0 = time.perf_counter()
+        fn(A[:rows_used], B)
+        dt_s = time.perf_counter() - t0
         if i >= args.warmup:
-            tfl.append(t)
+            tfl.append(2.0 * rows_used * n * k / dt_s / 1e12)
     value = statistics.mean(tfl)
     flops_full = 2.0 * m * n * k
     line = {
