@@ -152,7 +152,8 @@ def test_sgemm_golden(vk, name):
     assert v0.max_elem_rel(c[z["rows"]], z["C"]) <= ELEM
 
 
-@pytest.mark.parametrize("shape", [(1, 1, 1), (130, 131, 17), (257, 129, 64), (128, 256, 1000)])
+@pytest.mark.parametrize("shape", [(1, 1, 1), (130, 131, 17), (257, 129, 64), (128, 256, 1000), (300, 200, 20),
+                                   (129, 260, 36), (1000, 1000, 4), (64, 4, 1004)])
 def test_sgemm_ragged(vk, shape):
     m, n, k = shape
     A, B = v0.make_inputs(m, n, k, 31, dist="normal", dtype=np.float32)
@@ -161,6 +162,23 @@ def test_sgemm_ragged(vk, shape):
     c = C.cpu().numpy()
     g = v0.v0_f32(A, B)
     assert v0.rel_frobenius(c, g) <= FROB_SGEMM
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1000, 1000, 1000), (300, 200, 20)])
+def test_sgemm_v1_and_v2_agree(vk, shape):
+    m, n, k = shape
+    A, B = v0.make_inputs(m, n, k, 32, dist="normal", dtype=np.float32)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    c2 = vk.gemm(dA, dB)
+    try:
+        vk.set_option("sgemm_v2", 0)
+        c1 = vk.gemm(dA, dB)
+    finally:
+        vk.set_option("sgemm_v2", 1)
+    torch.cuda.synchronize()
+    g = v0.v0_f32(A, B)
+    for c in (c1, c2):
+        assert v0.rel_frobenius(c.cpu().numpy(), g) <= FROB_SGEMM
 
 
 @pytest.mark.parametrize("dtype", ["f16", "f32"])

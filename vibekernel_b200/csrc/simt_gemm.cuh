@@ -1,5 +1,7 @@
 // CUDA-core kernels:
-//   * sgemm_ffma_kernel  -- fp32 SGEMM (the reference has only a cBLAS v0 and a library call for
+//   * sgemm_ffma_v2_kernel -- the default fp32 SGEMM (cp.async 3-stage pipeline, below);
+//   * sgemm_ffma_kernel  -- fp32 SGEMM for operands the v2 kernel's 16-byte copies cannot take
+//     (the reference has only a cBLAS v0 and a library call for
 //     fp32: results/naive/src/matmul_f32/matmul_f32_v0_cblas.cpp:8-12,
 //     results/naive_no_ncu/src/matmul_f32/matmul_f32_v1_cuda-core.cu:10-16).  128 x 128 CTA tile,
 //     8 x 8 outputs per thread in four 4 x 4 quadrants, 128-bit global loads, A staged
@@ -9,6 +11,7 @@
 //   * fill_zero_kernel   -- C = 0 for k == 0.
 #pragma once
 
+#include <cstdint>
 #include <cuda_fp16.h>
 
 namespace vk {
@@ -121,6 +124,132 @@ __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_kernel(const SgemmPa
         }
         __syncthreads();
     }
+
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int row = m0 + ty * 4 + (i & 3) + (i >> 2) * 64;
+        if (row >= p.M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int col = n0 + tx * 4 + h * 64;
+            float* dst = p.C + row * p.ldc + col;
+            if (p.vec_c && col + 3 < p.N) {
+                *reinterpret_cast<float4*>(dst) =
+                    make_float4(acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (col + j < p.N) dst[j] = acc[i][4 * h + j];
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// sgemm_ffma_v2_kernel -- the default fp32 SGEMM for 16-byte-aligned A/B with lda, ldb multiples
+// of 4.  128 x 128 CTA tile, BK = 16, 256 threads, 8 x 8 outputs per thread in four 4 x 4
+// quadrants.  Operands move global -> shared with cp.async (16-byte, zero-filled at the edges) in a
+// 3-stage ring, so no registers stage the next tile and three k-tiles are in flight.  A stays
+// K-contiguous in shared memory (rows padded to 20 floats so the two rows a warp reads per
+// 128-bit load sit in different banks); per 4-deep k chunk a thread loads its 8 A rows and 4 B
+// rows with 16 vector loads and issues 256 FFMAs.
+constexpr int kSg2BK = 16, kSg2Stages = 3, kSg2APitch = kSg2BK + 4;
+constexpr int kSg2AFloats = kSgBM * kSg2APitch, kSg2BFloats = kSg2BK * kSgBN;
+constexpr int kSg2SmemBytes = kSg2Stages * (kSg2AFloats + kSg2BFloats) * 4;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void sg2_load_stage(const SgemmParams& p, float* As, float* Bs, int m0, int n0, int k0)
+{
+    const int t = threadIdx.x;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        // A: 128 rows x 16 k = 512 float4, four per row
+        const int f = t + i * 256;
+        const int row = f >> 2, kq = (f & 3) * 4;
+        const int gr = m0 + row, gk = k0 + kq;
+        int bytes = 0;
+        const float* src = p.A;
+        if (gr < p.M && gk < p.K) {
+            bytes = min(4, p.K - gk) * 4;
+            src = p.A + static_cast<long long>(gr) * p.lda + gk;
+        }
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(As + row * kSg2APitch + kq)), src, bytes);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        // B: 16 k-rows x 128 columns = 512 float4, 32 per row
+        const int f = t + i * 256;
+        const int row = f >> 5, cq = (f & 31) * 4;
+        const int gk = k0 + row, gc = n0 + cq;
+        int bytes = 0;
+        const float* src = p.B;
+        if (gk < p.K && gc < p.N) {
+            bytes = min(4, p.N - gc) * 4;
+            src = p.B + static_cast<long long>(gk) * p.ldb + gc;
+        }
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(Bs + row * kSgBN + cq)), src, bytes);
+    }
+}
+
+__global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_v2_kernel(const SgemmParams p)
+{
+    extern __shared__ __align__(16) float sg2_smem[];
+    float* As = sg2_smem;                            // [stage][128][20]
+    float* Bs = sg2_smem + kSg2Stages * kSg2AFloats; // [stage][16][128]
+    const int t = threadIdx.x;
+    const int tx = t & 15, ty = t >> 4;
+    const int m0 = blockIdx.y * kSgBM, n0 = blockIdx.x * kSgBN;
+    const int nk = (p.K + kSg2BK - 1) / kSg2BK;
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+#pragma unroll
+    for (int s = 0; s < kSg2Stages - 1; ++s) {
+        if (s < nk) sg2_load_stage(p, As + s * kSg2AFloats, Bs + s * kSg2BFloats, m0, n0, s * kSg2BK);
+        cp_async_commit();
+    }
+    for (int kt = 0; kt < nk; ++kt) {
+        cp_async_wait<kSg2Stages - 2>();
+        __syncthreads();  // stage kt landed for all threads; stage kt-1 is free for the next load
+        const int nxt = kt + kSg2Stages - 1;
+        if (nxt < nk)
+            sg2_load_stage(p, As + (nxt % kSg2Stages) * kSg2AFloats, Bs + (nxt % kSg2Stages) * kSg2BFloats, m0, n0,
+                           nxt * kSg2BK);
+        cp_async_commit();
+        const float* a_s = As + (kt % kSg2Stages) * kSg2AFloats;
+        const float* b_s = Bs + (kt % kSg2Stages) * kSg2BFloats;
+#pragma unroll
+        for (int kc = 0; kc < kSg2BK; kc += 4) {
+            float4 a4[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                a4[i] = *reinterpret_cast<const float4*>(a_s + (ty * 4 + (i & 3) + (i >> 2) * 64) * kSg2APitch + kc);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const float4 b0 = *reinterpret_cast<const float4*>(b_s + (kc + kk) * kSgBN + tx * 4);
+                const float4 b1 = *reinterpret_cast<const float4*>(b_s + (kc + kk) * kSgBN + tx * 4 + 64);
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float av = kk == 0 ? a4[i].x : kk == 1 ? a4[i].y : kk == 2 ? a4[i].z : a4[i].w;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av, bv[j], acc[i][j]);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {

@@ -114,6 +114,7 @@ static std::atomic<int> g_raster_group{8};
 // to both CTAs' "empty" barriers, and those commits measurably throttle the tensor pipe; 128-deep
 // stages (3 x 64 KB) halve them per MMA and beat 64-deep ones (6 x 32 KB) at every size measured.
 static std::atomic<int> g_bk_2sm256{128};
+static std::atomic<int> g_sgemm_v2{1};
 static std::atomic<int> g_clock_probe_on{0};
 static std::atomic<int> g_trace_on{0};
 
@@ -424,7 +425,20 @@ static int launch_sgemm(const Problem& pb)
     p.vec_c = (reinterpret_cast<uintptr_t>(pb.C) % 16 == 0) && (pb.ldc % 4 == 0);
     dim3 grid(static_cast<unsigned>((pb.n + kSgBN - 1) / kSgBN), static_cast<unsigned>((pb.m + kSgBM - 1) / kSgBM));
     if (grid.y > 65535u) return set_error(VK_ERR_UNSUPPORTED, "m too large for the SGEMM grid");
-    sgemm_ffma_kernel<<<grid, kSgThreads, 0, pb.stream>>>(p);
+    if (p.vec_a && p.vec_b && g_sgemm_v2.load(std::memory_order_relaxed)) {
+        static std::atomic<int> attr_dev_mask{0};  // smem attribute set once per device (bit per ordinal < 31)
+        int dev = 0;
+        VK_CUDA_TRY(cudaGetDevice(&dev));
+        const int bit = 1 << (dev & 31);
+        if (!(attr_dev_mask.load() & bit)) {
+            VK_CUDA_TRY(cudaFuncSetAttribute(sgemm_ffma_v2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSg2SmemBytes));
+            attr_dev_mask.fetch_or(bit);
+        }
+        sgemm_ffma_v2_kernel<<<grid, kSgThreads, kSg2SmemBytes, pb.stream>>>(p);
+    } else {
+        sgemm_ffma_kernel<<<grid, kSgThreads, 0, pb.stream>>>(p);
+    }
     VK_CUDA_TRY(cudaGetLastError());
     return VK_OK;
 }
@@ -738,6 +752,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
     if (strcmp(name, "bk_2sm256") == 0) {
         if (value != 64 && value != 128) return set_error(VK_ERR_INVALID_ARGUMENT, "bk_2sm256 must be 64 or 128");
         g_bk_2sm256.store(static_cast<int>(value));
+        return VK_OK;
+    }
+    if (strcmp(name, "sgemm_v2") == 0) {
+        g_sgemm_v2.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
     if (strcmp(name, "trace") == 0) {
