@@ -81,6 +81,30 @@ typedef struct vk_gemm_args {
  * The general entry point.  Asynchronous; returns before the kernel finishes. */
 int vk_gemm(const vk_gemm_args* args);
 
+/* Extensions beyond the reference's NN, alpha = 1, beta = 0 contract (no counterpart in the
+ * reference; the survey's "next" rows: generic layouts and epilogue fusion):
+ *   C = act(alpha * op(A) * op(B) + beta * C_in + bias)
+ * op(A) = A (stored m x k, lda >= k) or, with trans_a, A^T of a matrix stored k x m (lda >= m);
+ * op(B) = B (stored k x n, ldb >= n) or, with trans_b, B^T of a matrix stored n x k (ldb >= k).
+ * C_in (m x n, leading dimension ldc_in, 0 = ldc; may be C itself) is read when beta != 0; bias is
+ * a length-n row vector broadcast over rows; both have C's element type.  The epilogue runs in
+ * fp32 before the single rounding to the output type.  Transposed operands: fp16 only.  The
+ * tensor-core kernels take all four layouts when the stored matrices meet the TMA rule (16-byte
+ * aligned, leading dimension a multiple of 8); otherwise VK_ALGO_AUTO uses the predicated kernel. */
+typedef enum vk_activation { VK_ACT_NONE = 0, VK_ACT_RELU = 1 } vk_activation;
+
+typedef struct vk_gemm_ext {
+    int32_t trans_a, trans_b;
+    float alpha, beta;
+    const void* C_in;
+    int64_t ldc_in;
+    const void* bias;
+    int32_t activation; /* vk_activation */
+} vk_gemm_ext;
+
+/* vk_gemm with the extensions above; ext == NULL is exactly vk_gemm. */
+int vk_gemm_ex(const vk_gemm_args* args, const vk_gemm_ext* ext);
+
 /* No counterpart in the reference.  Same contract as vk_gemm for the fp16 tensor-core kernels
  * (algo AUTO, TC_2SM or TC_1SM; 16-byte aligned A/B with lda, ldb multiples of 8), for callers
  * that cannot allocate device memory: code running during CUDA graph capture, applications whose

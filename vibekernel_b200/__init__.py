@@ -39,7 +39,7 @@ EXPORTED = (
     "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
     "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
-    "vk_gemm_host",
+    "vk_gemm_host", "vk_gemm_ex",
 )
 
 
@@ -57,6 +57,16 @@ class GemmArgs(ctypes.Structure):
         ("dtype", ctypes.c_int32), ("acc", ctypes.c_int32), ("algo", ctypes.c_int32), ("tile_n", ctypes.c_int32),
         ("stream", ctypes.c_void_p),
     ]
+
+
+class GemmExt(ctypes.Structure):
+    _fields_ = [
+        ("trans_a", ctypes.c_int32), ("trans_b", ctypes.c_int32), ("alpha", ctypes.c_float), ("beta", ctypes.c_float),
+        ("C_in", ctypes.c_void_p), ("ldc_in", ctypes.c_int64), ("bias", ctypes.c_void_p), ("activation", ctypes.c_int32),
+    ]
+
+
+ACT_NONE, ACT_RELU = 0, 1
 
 
 class ShardArgs(ctypes.Structure):
@@ -82,6 +92,8 @@ def _load() -> ctypes.CDLL:
     lib.vk_gemm_noalloc.restype = ctypes.c_int
     lib.vk_gemm_host.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_int32]
     lib.vk_gemm_host.restype = ctypes.c_int
+    lib.vk_gemm_ex.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(GemmExt)]
+    lib.vk_gemm_ex.restype = ctypes.c_int
     sz = ctypes.c_size_t
     lib.vk_matmul_f16.argtypes = [ctypes.c_int, sz, sz, sz, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.vk_matmul_f16.restype = ctypes.c_int
@@ -141,22 +153,24 @@ def _stream_handle(stream) -> int | None:
 
 def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile_n: int = 0,
          stream=None, lda: int = 0, ldb: int = 0, ldc: int = 0, m: int | None = None,
-         n: int | None = None, k: int | None = None):
-    """C = A @ B on the GPU through ``vk_gemm``.
+         n: int | None = None, k: int | None = None, trans_a: bool = False, trans_b: bool = False,
+         alpha: float = 1.0, beta: float = 0.0, c_in=None, bias=None, act: str | None = None):
+    """C = act(alpha * op(A) @ op(B) + beta * c_in + bias) on the GPU (``vk_gemm`` / ``vk_gemm_ex``).
 
-    A [m, k] and B [k, n] are CUDA tensors (fp16, or fp32 for the FFMA kernel), row-major with
-    unit column stride; a row stride larger than the row length is passed as lda/ldb.  Returns C
-    (allocated if not given).  ``c_f32``: optional fp32 [m, n] tensor receiving the result before
-    rounding (fp16 only).  Asynchronous on ``stream`` (default: torch's current stream).
+    A is [m, k] (or [k, m] with ``trans_a``) and B is [k, n] (or [n, k] with ``trans_b``), CUDA
+    tensors (fp16, or fp32 for the FFMA kernel) with unit column stride; a row stride larger than
+    the row length is passed on as lda/ldb.  Returns C (allocated if not given).  ``c_f32``:
+    optional fp32 [m, n] tensor receiving the result before rounding (fp16 only).  ``act``: None
+    or "relu".  Asynchronous on ``stream`` (default: torch's current stream).
     """
     import torch
     if A.dtype not in (torch.float16, torch.float32) or B.dtype != A.dtype:
         raise TypeError("A and B must both be float16 or both float32")
     if not (A.is_cuda and B.is_cuda):
         raise ValueError("A and B must be CUDA tensors (no CPU fallback)")
-    m = A.shape[0] if m is None else m
-    k = A.shape[1] if k is None else k
-    n = B.shape[1] if n is None else n
+    m = (A.shape[1] if trans_a else A.shape[0]) if m is None else m
+    k = (A.shape[0] if trans_a else A.shape[1]) if k is None else k
+    n = (B.shape[0] if trans_b else B.shape[1]) if n is None else n
     if A.dim() != 2 or B.dim() != 2 or A.stride(1) != 1 or B.stride(1) != 1:
         raise ValueError("A and B must be 2-D with unit column stride")
     lda = lda or A.stride(0)
@@ -178,8 +192,24 @@ def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile
     a.algo = _ALGOS[algo]
     a.tile_n = tile_n
     a.stream = _stream_handle(stream)
+    extended = trans_a or trans_b or alpha != 1.0 or beta != 0.0 or bias is not None or act is not None
     with torch.cuda.device(A.device):
-        check(lib.vk_gemm(ctypes.byref(a)))
+        if not extended:
+            check(lib.vk_gemm(ctypes.byref(a)))
+            return C
+        x = GemmExt()
+        x.trans_a, x.trans_b = int(bool(trans_a)), int(bool(trans_b))
+        x.alpha, x.beta = float(alpha), float(beta)
+        if c_in is not None:
+            if c_in.dtype != C.dtype or c_in.dim() != 2 or c_in.stride(1) != 1:
+                raise ValueError("c_in must be 2-D, unit column stride, same dtype as C")
+            x.C_in, x.ldc_in = c_in.data_ptr(), c_in.stride(0)
+        if bias is not None:
+            if bias.dtype != C.dtype or not bias.is_contiguous() or bias.numel() < n:
+                raise ValueError("bias must be a contiguous vector of length n with C's dtype")
+            x.bias = bias.data_ptr()
+        x.activation = {None: ACT_NONE, "relu": ACT_RELU}[act]
+        check(lib.vk_gemm_ex(ctypes.byref(a), ctypes.byref(x)))
     return C
 
 

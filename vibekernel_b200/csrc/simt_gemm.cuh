@@ -25,7 +25,39 @@ struct SgemmParams {
     float* C;
     long long ldc;
     int vec_a, vec_b, vec_c;  // 16-byte vector access allowed (alignment of base and ld)
+    // fused epilogue (ep = 1): C = act(alpha * acc + beta * C_in + bias); act 1 = relu
+    int ep, act;
+    float alpha, beta;
+    const float* Cin;
+    long long ldcin;
+    const float* bias;
 };
+
+// Stores four consecutive results of one row (col .. col+3), applying the fused epilogue.
+__device__ __forceinline__ void sg_store4(const SgemmParams& p, int row, int col, float v0, float v1, float v2,
+                                          float v3)
+{
+    float v[4] = {v0, v1, v2, v3};
+    if (p.ep) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (col + j >= p.N) continue;
+            float x = p.alpha * v[j];
+            if (p.Cin != nullptr && p.beta != 0.f) x = fmaf(p.beta, p.Cin[row * p.ldcin + col + j], x);
+            if (p.bias != nullptr) x += p.bias[col + j];
+            if (p.act == 1) x = fmaxf(x, 0.f);
+            v[j] = x;
+        }
+    }
+    float* dst = p.C + row * p.ldc + col;
+    if (p.vec_c && col + 3 < p.N) {
+        *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (col + j < p.N) dst[j] = v[j];
+    }
+}
 
 constexpr int kSgBM = 128, kSgBN = 128, kSgBK = 8, kSgThreads = 256;
 constexpr int kSgAPad = 4;  // As row padding (floats): transposed stores hit distinct banks
@@ -132,15 +164,8 @@ __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_kernel(const SgemmPa
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int col = n0 + tx * 4 + h * 64;
-            float* dst = p.C + row * p.ldc + col;
-            if (p.vec_c && col + 3 < p.N) {
-                *reinterpret_cast<float4*>(dst) =
-                    make_float4(acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (col + j < p.N) dst[j] = acc[i][4 * h + j];
-            }
+            if (col < p.N)
+                sg_store4(p, row, col, acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
         }
     }
 }
@@ -258,15 +283,8 @@ __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_v2_kernel(const Sgem
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int col = n0 + tx * 4 + h * 64;
-            float* dst = p.C + row * p.ldc + col;
-            if (p.vec_c && col + 3 < p.N) {
-                *reinterpret_cast<float4*>(dst) =
-                    make_float4(acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (col + j < p.N) dst[j] = acc[i][4 * h + j];
-            }
+            if (col < p.N)
+                sg_store4(p, row, col, acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
         }
     }
 }
@@ -281,6 +299,12 @@ struct HgemmSimtParams {
     __half* C;
     long long ldc;
     float* C32;  // optional fp32 copy, ld = N
+    int trans_a, trans_b;  // A stored k x m / B stored n x k (row-major) when set
+    int ep, act;           // fused epilogue, as in SgemmParams
+    float alpha, beta;
+    const __half* Cin;
+    long long ldcin;
+    const __half* bias;
 };
 
 constexpr int kHsTile = 64, kHsBK = 16;
@@ -298,10 +322,12 @@ __global__ void __launch_bounds__(256) hgemm_simt_kernel(const HgemmSimtParams p
         for (int e = t; e < kHsTile * kHsBK; e += 256) {
             const int r = e / kHsBK, c = e % kHsBK;  // A: row r, k c
             const int gr = m0 + r, gk = k0 + c;
-            As[c][r] = (gr < p.M && gk < p.K) ? __half2float(p.A[gr * p.lda + gk]) : 0.f;
+            As[c][r] = (gr < p.M && gk < p.K)
+                           ? __half2float(p.trans_a ? p.A[gk * p.lda + gr] : p.A[gr * p.lda + gk]) : 0.f;
             const int kr = e / kHsTile, nc = e % kHsTile;  // B: k kr, col nc
             const int bk = k0 + kr, bn = n0 + nc;
-            Bs[kr][nc] = (bk < p.K && bn < p.N) ? __half2float(p.B[bk * p.ldb + bn]) : 0.f;
+            Bs[kr][nc] = (bk < p.K && bn < p.N)
+                             ? __half2float(p.trans_b ? p.B[bn * p.ldb + bk] : p.B[bk * p.ldb + bn]) : 0.f;
         }
         __syncthreads();
 #pragma unroll
@@ -326,8 +352,15 @@ __global__ void __launch_bounds__(256) hgemm_simt_kernel(const HgemmSimtParams p
         for (int j = 0; j < 4; ++j) {
             const int col = n0 + tx + 16 * j;
             if (col >= p.N) continue;
-            p.C[row * p.ldc + col] = __float2half_rn(acc[i][j]);
-            if (p.C32 != nullptr) p.C32[static_cast<long long>(row) * p.N + col] = acc[i][j];
+            float v = acc[i][j];
+            if (p.ep) {
+                v *= p.alpha;
+                if (p.Cin != nullptr && p.beta != 0.f) v = fmaf(p.beta, __half2float(p.Cin[row * p.ldcin + col]), v);
+                if (p.bias != nullptr) v += __half2float(p.bias[col]);
+                if (p.act == 1) v = fmaxf(v, 0.f);
+            }
+            p.C[row * p.ldc + col] = __float2half_rn(v);
+            if (p.C32 != nullptr) p.C32[static_cast<long long>(row) * p.N + col] = v;
         }
     }
 }
@@ -342,6 +375,24 @@ __global__ void fill_zero_kernel(T* C, long long ldc, int M, int N, float* C32)
         const long long r = i / N, c = i % N;
         C[r * ldc + c] = T(0.f);
         if (C32 != nullptr) C32[i] = 0.f;
+    }
+}
+
+// k == 0 with a fused epilogue: C = act(beta * C_in + bias).
+template <typename T>
+__global__ void epilogue_only_kernel(T* C, long long ldc, int M, int N, float* C32, const T* Cin, long long ldcin,
+                                     float beta, const T* bias, int act)
+{
+    const long long total = static_cast<long long>(M) * N;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / N, c = i % N;
+        float v = 0.f;
+        if (Cin != nullptr && beta != 0.f) v = beta * static_cast<float>(Cin[r * ldcin + c]);
+        if (bias != nullptr) v += static_cast<float>(bias[c]);
+        if (act == 1) v = fmaxf(v, 0.f);
+        C[r * ldc + c] = T(v);
+        if (C32 != nullptr) C32[i] = v;
     }
 }
 

@@ -57,7 +57,35 @@ struct TcParams {
     int* counters;           // arrival counters: [tail tile][CTA rank][4 epilogue warps]
     int clock_probe;         // 1: CTA 0 accumulates (cycles, ns, launches) into g_clock_probe
     int trace;               // 1: record the launch timeline into g_trace
+    // operand layouts: a_mn = A stored k x m (A^T row-major: M-major tiles); b_k = B stored n x k
+    // (B^T row-major: K-major tiles).  Default (0, 0) is the reference's NN row-major convention.
+    int a_mn, b_k;
+    // fused epilogue (ep = 1): C = act(alpha * acc + beta * C_in + bias), act 0 = none, 1 = relu
+    int ep, act;
+    float alpha, beta;
+    const __half* Cin;
+    long long ldcin;
+    const __half* bias;
 };
+
+// Fused epilogue for one row's 32 fp32 results at columns col .. col+31 (fp32 math, then round).
+__device__ __forceinline__ void store_chunk_fused(const TcParams& p, int row, int col, float (&f)[32])
+{
+    if (row >= p.M) return;
+    __half* crow = p.C + static_cast<long long>(row) * p.ldc;
+    const __half* cin = p.Cin ? p.Cin + static_cast<long long>(row) * p.ldcin : nullptr;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        if (col + i < p.N) {
+            float v = p.alpha * f[i];
+            if (cin != nullptr && p.beta != 0.f) v = fmaf(p.beta, __half2float(cin[col + i]), v);
+            if (p.bias != nullptr) v += __half2float(p.bias[col + i]);
+            if (p.act == 1) v = fmaxf(v, 0.f);
+            crow[col + i] = __float2half_rn(v);
+            if (p.C32 != nullptr) p.C32[static_cast<long long>(row) * p.N + col + i] = v;
+        }
+    }
+}
 
 struct Unit {
     int tile, kb0, kb1, slice;  // slice < 0: whole tile
@@ -91,8 +119,10 @@ struct TcCfg {
     static constexpr int kBBytes = kBNCta * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kBBoxes = kBNCta / 64;  // 64-column TMA boxes of B per stage
-    static constexpr int kABox = kBM * 64 * 2;   // bytes of one 64-wide k-span of A (128 rows)
-    static constexpr int kBBox = 64 * kBK * 2;   // bytes of one 64-column box of B (kBK rows)
+    static constexpr int kABox = kBM * 64 * 2;   // bytes of one 64-wide k-span of K-major A (128 rows)
+    static constexpr int kAMnBox = 64 * kBK * 2; // bytes of one 64-row box of M-major A (kBK k rows)
+    static constexpr int kBBox = 64 * kBK * 2;   // bytes of one 64-column box of N-major B (kBK rows)
+    static constexpr int kBKBox = kBNCta * 64 * 2; // bytes of one 64-wide k-span of K-major B
     static constexpr int kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                    : (2 * BN <= 256) ? 256 : 512;
     static constexpr int kNumBars = 2 * STAGES + 4 + 4;  // + one reduction barrier per epilogue warp
@@ -132,6 +162,18 @@ template <bool ACC_F32>
 __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col, const uint32_t (&r)[32])
 {
     if (row >= p.M) return;
+    if (p.ep) {
+        float f[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if constexpr (ACC_F32)
+                f[i] = __uint_as_float(r[i]);
+            else
+                f[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(r[i])));
+        }
+        store_chunk_fused(p, row, col, f);
+        return;
+    }
     __half* crow = p.C + static_cast<long long>(row) * p.ldc;
     const bool full = (col + 32 <= p.N) && p.vec_ok;
     if (full) {
@@ -276,22 +318,32 @@ __global__ void __launch_bounds__(192, 1)
                     const uint32_t a_dst = smem_u32(sA + stage * Cfg::kABytes);
                     const uint32_t b_dst = smem_u32(sB + stage * Cfg::kBBytes);
                     const int k0 = kb * Cfg::kBK;
+                    uint32_t bar = fb;
                     if constexpr (CG == 1) {
                         mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-#pragma unroll
-                        for (int a = 0; a < KA; ++a) tma_load_2d(a_dst + a * Cfg::kABox, &tmap_a, fb, k0 + 64 * a, m0);
-#pragma unroll
-                        for (int j = 0; j < Cfg::kBBoxes; ++j)
-                            tma_load_2d(b_dst + j * Cfg::kBBox, &tmap_b, fb, n0 + 64 * j, k0);
                     } else {
                         if (rank == 0) mbar_arrive_expect_tx(fb, 2 * Cfg::kStageBytes);
-                        const uint32_t fb_leader = mapa_shared(fb, 0);
+                        bar = mapa_shared(fb, 0);
+                    }
+                    auto load = [&](uint32_t dst, const CUtensorMap* map, int c0, int c1) {
+                        if constexpr (CG == 1)
+                            tma_load_2d(dst, map, bar, c0, c1);
+                        else
+                            tma_load_2d_pair(dst, map, bar, c0, c1);
+                    };
+                    if (!p.a_mn) {
 #pragma unroll
-                        for (int a = 0; a < KA; ++a)
-                            tma_load_2d_pair(a_dst + a * Cfg::kABox, &tmap_a, fb_leader, k0 + 64 * a, m0);
+                        for (int a = 0; a < KA; ++a) load(a_dst + a * Cfg::kABox, &tmap_a, k0 + 64 * a, m0);
+                    } else {
 #pragma unroll
-                        for (int j = 0; j < Cfg::kBBoxes; ++j)
-                            tma_load_2d_pair(b_dst + j * Cfg::kBBox, &tmap_b, fb_leader, n0 + 64 * j, k0);
+                        for (int j = 0; j < BM / 64; ++j) load(a_dst + j * Cfg::kAMnBox, &tmap_a, m0 + 64 * j, k0);
+                    }
+                    if (!p.b_k) {
+#pragma unroll
+                        for (int j = 0; j < Cfg::kBBoxes; ++j) load(b_dst + j * Cfg::kBBox, &tmap_b, n0 + 64 * j, k0);
+                    } else {
+#pragma unroll
+                        for (int a = 0; a < KA; ++a) load(b_dst + a * Cfg::kBKBox, &tmap_b, k0 + 64 * a, n0);
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -314,10 +366,13 @@ __global__ void __launch_bounds__(192, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
         if (rank == 0 && lane == 0) {
-            constexpr uint32_t kIdesc = idesc_f16(BM * CG, BN, ACC_F32, /*b_mn_major=*/true);
-            // B is N-major: 64-column atoms of BK rows x 128 B; LBO steps between atoms, SBO
-            // between 8-row groups.  A is K-major: SBO steps between 8-row groups.
-            constexpr uint32_t kBLbo = Cfg::kBK * 128;
+            // M/N-major operands: 64-element atoms of BK rows x 128 B, LBO steps between atoms and
+            // SBO between 8-row groups, k advances 16 rows (2 KB) per MMA.  K-major operands: rows of
+            // 128 B in 8-row groups (SBO), k advances 32 B within a 64-wide span and a whole span
+            // (box) every 4 MMAs.
+            const uint32_t idesc = idesc_f16(BM * CG, BN, ACC_F32, /*b_mn_major=*/!p.b_k) |
+                                   (p.a_mn ? (1u << 15) : 0u);
+            constexpr uint32_t kMnLbo = Cfg::kBK * 128;
             int stage = 0;
             uint32_t phase = 0;
             int it = 0;
@@ -340,9 +395,13 @@ __global__ void __launch_bounds__(192, 1)
                     const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
 #pragma unroll
                     for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
-                        const uint64_t a_desc = smem_desc_sw128(a_addr + (kk >> 2) * Cfg::kABox + (kk & 3) * 32, 16, 1024);
-                        const uint64_t b_desc = smem_desc_sw128(b_addr + kk * 16 * 128, kBLbo, 1024);
-                        umma_f16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
+                        const uint64_t a_desc =
+                            p.a_mn ? smem_desc_sw128(a_addr + kk * 16 * 128, kMnLbo, 1024)
+                                   : smem_desc_sw128(a_addr + (kk >> 2) * Cfg::kABox + (kk & 3) * 32, 16, 1024);
+                        const uint64_t b_desc =
+                            p.b_k ? smem_desc_sw128(b_addr + (kk >> 2) * Cfg::kBKBox + (kk & 3) * 32, 16, 1024)
+                                  : smem_desc_sw128(b_addr + kk * 16 * 128, kMnLbo, 1024);
+                        umma_f16<CG>(d_tmem, a_desc, b_desc, idesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
                     }
                     const uint32_t eb = empty_bar(stage);
                     umma_commit<CG>(eb);

@@ -314,6 +314,13 @@ struct Problem {
     int64_t m, n, k, lda, ldb, ldc;
     cudaStream_t stream;
     int tile_n;
+    // vk_gemm_ex extensions (all off for vk_gemm)
+    int trans_a = 0, trans_b = 0;
+    int ep = 0, act = 0;
+    float alpha = 1.f, beta = 0.f;
+    const void* Cin = nullptr;
+    int64_t ldcin = 0;
+    const void* bias = nullptr;
 };
 
 template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
@@ -326,9 +333,13 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     if (rc != VK_OK) return rc;
 
     CUtensorMap ta, tb;
-    rc = make_tmap_f16(&ta, pb.A, pb.m, pb.k, pb.lda, 64, Cfg::kBM);
+    // A: K-major boxes of 64 k x 128 rows, or (A stored k x m) M-major boxes of 64 rows x BK k.
+    // B: N-major boxes of 64 columns x BK k, or (B stored n x k) K-major boxes of 64 k x BN/CG rows.
+    rc = pb.trans_a ? make_tmap_f16(&ta, pb.A, pb.k, pb.m, pb.lda, 64, Cfg::kBK)
+                    : make_tmap_f16(&ta, pb.A, pb.m, pb.k, pb.lda, 64, Cfg::kBM);
     if (rc != VK_OK) return rc;
-    rc = make_tmap_f16(&tb, pb.B, pb.k, pb.n, pb.ldb, 64, Cfg::kBK);
+    rc = pb.trans_b ? make_tmap_f16(&tb, pb.B, pb.n, pb.k, pb.ldb, 64, Cfg::kBNCta)
+                    : make_tmap_f16(&tb, pb.B, pb.k, pb.n, pb.ldb, 64, Cfg::kBK);
     if (rc != VK_OK) return rc;
 
     TcParams p;
@@ -347,6 +358,15 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     p.vec_ok = (c_vec && c32_vec) ? 1 : 0;
     p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
     p.clock_probe = g_clock_probe_on.load(std::memory_order_relaxed);
+    p.a_mn = pb.trans_a;
+    p.b_k = pb.trans_b;
+    p.ep = pb.ep;
+    p.act = pb.act;
+    p.alpha = pb.alpha;
+    p.beta = pb.beta;
+    p.Cin = static_cast<const __half*>(pb.Cin);
+    p.ldcin = pb.ldcin;
+    p.bias = static_cast<const __half*>(pb.bias);
     p.trace = g_trace_on.load(std::memory_order_relaxed);
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
@@ -423,6 +443,13 @@ static int launch_sgemm(const Problem& pb)
     p.vec_a = (reinterpret_cast<uintptr_t>(pb.A) % 16 == 0) && (pb.lda % 4 == 0);
     p.vec_b = (reinterpret_cast<uintptr_t>(pb.B) % 16 == 0) && (pb.ldb % 4 == 0);
     p.vec_c = (reinterpret_cast<uintptr_t>(pb.C) % 16 == 0) && (pb.ldc % 4 == 0);
+    p.ep = pb.ep;
+    p.act = pb.act;
+    p.alpha = pb.alpha;
+    p.beta = pb.beta;
+    p.Cin = static_cast<const float*>(pb.Cin);
+    p.ldcin = pb.ldcin;
+    p.bias = static_cast<const float*>(pb.bias);
     dim3 grid(static_cast<unsigned>((pb.n + kSgBN - 1) / kSgBN), static_cast<unsigned>((pb.m + kSgBM - 1) / kSgBM));
     if (grid.y > 65535u) return set_error(VK_ERR_UNSUPPORTED, "m too large for the SGEMM grid");
     if (p.vec_a && p.vec_b && g_sgemm_v2.load(std::memory_order_relaxed)) {
@@ -456,6 +483,15 @@ static int launch_hgemm_simt(const Problem& pb)
     p.ldb = pb.ldb;
     p.ldc = pb.ldc;
     p.C32 = pb.C32;
+    p.trans_a = pb.trans_a;
+    p.trans_b = pb.trans_b;
+    p.ep = pb.ep;
+    p.act = pb.act;
+    p.alpha = pb.alpha;
+    p.beta = pb.beta;
+    p.Cin = static_cast<const __half*>(pb.Cin);
+    p.ldcin = pb.ldcin;
+    p.bias = static_cast<const __half*>(pb.bias);
     dim3 grid(static_cast<unsigned>((pb.n + kHsTile - 1) / kHsTile), static_cast<unsigned>((pb.m + kHsTile - 1) / kHsTile));
     if (grid.y > 65535u) return set_error(VK_ERR_UNSUPPORTED, "m too large for the SIMT grid");
     hgemm_simt_kernel<<<grid, 256, 0, pb.stream>>>(p);
@@ -469,8 +505,15 @@ static int launch_zero(DeviceState& st, const Problem& pb)
     const long long total = pb.m * pb.n;
     long long blocks = (total + 255) / 256;
     if (blocks > 8LL * st.sm_count) blocks = 8LL * st.sm_count;
-    fill_zero_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, pb.stream>>>(
-        static_cast<T*>(pb.C), pb.ldc, static_cast<int>(pb.m), static_cast<int>(pb.n), pb.C32);
+    if (pb.ep) {
+        // k == 0: the product is zero, the epilogue still applies (beta * C_in + bias, activation)
+        epilogue_only_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, pb.stream>>>(
+            static_cast<T*>(pb.C), pb.ldc, static_cast<int>(pb.m), static_cast<int>(pb.n), pb.C32,
+            static_cast<const T*>(pb.Cin), pb.ldcin, pb.beta, static_cast<const T*>(pb.bias), pb.act);
+    } else {
+        fill_zero_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, pb.stream>>>(
+            static_cast<T*>(pb.C), pb.ldc, static_cast<int>(pb.m), static_cast<int>(pb.n), pb.C32);
+    }
     VK_CUDA_TRY(cudaGetLastError());
     return VK_OK;
 }
@@ -510,21 +553,29 @@ void release_device_state()
 // ==========================================================================================
 using namespace vk;
 
-extern "C" int vk_gemm(const vk_gemm_args* a)
+static int gemm_entry(const vk_gemm_args* a, const vk_gemm_ext* x, const char* name)
 {
-    if (a == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: args is NULL");
+    if (a == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "%s: args is NULL", name);
     if (a->m < 0 || a->n < 0 || a->k < 0)
-        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: negative size m=%lld n=%lld k=%lld", (long long)a->m,
+        return set_error(VK_ERR_INVALID_ARGUMENT, "%s: negative size m=%lld n=%lld k=%lld", name, (long long)a->m,
                          (long long)a->n, (long long)a->k);
     const int64_t kMaxDim = (1LL << 31) - 1;
     if (a->m > kMaxDim || a->n > kMaxDim || a->k > kMaxDim)
-        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: dimensions above 2^31-1 are not supported");
+        return set_error(VK_ERR_UNSUPPORTED, "%s: dimensions above 2^31-1 are not supported", name);
     if (a->dtype != VK_DTYPE_F16 && a->dtype != VK_DTYPE_F32)
-        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: unknown dtype %d", a->dtype);
+        return set_error(VK_ERR_INVALID_ARGUMENT, "%s: unknown dtype %d", name, a->dtype);
     if (a->acc != VK_ACC_F32 && a->acc != VK_ACC_F16)
-        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: unknown acc %d", a->acc);
+        return set_error(VK_ERR_INVALID_ARGUMENT, "%s: unknown acc %d", name, a->acc);
     if (a->algo < VK_ALGO_AUTO || a->algo > VK_ALGO_SIMT)
-        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: unknown algo %d", a->algo);
+        return set_error(VK_ERR_INVALID_ARGUMENT, "%s: unknown algo %d", name, a->algo);
+    if (x != nullptr) {
+        if ((x->trans_a != 0 && x->trans_a != 1) || (x->trans_b != 0 && x->trans_b != 1))
+            return set_error(VK_ERR_INVALID_ARGUMENT, "%s: trans_a and trans_b must be 0 or 1", name);
+        if (x->activation != VK_ACT_NONE && x->activation != VK_ACT_RELU)
+            return set_error(VK_ERR_INVALID_ARGUMENT, "%s: unknown activation %d", name, x->activation);
+        if (x->beta != 0.f && x->C_in == nullptr)
+            return set_error(VK_ERR_INVALID_ARGUMENT, "%s: beta != 0 needs C_in", name);
+    }
 
     Problem pb;
     pb.A = a->A;
@@ -534,19 +585,37 @@ extern "C" int vk_gemm(const vk_gemm_args* a)
     pb.m = a->m;
     pb.n = a->n;
     pb.k = a->k;
-    pb.lda = a->lda ? a->lda : a->k;
-    pb.ldb = a->ldb ? a->ldb : a->n;
+    pb.trans_a = x ? x->trans_a : 0;
+    pb.trans_b = x ? x->trans_b : 0;
+    // row lengths of the stored matrices: A is m x k (k x m when transposed), B is k x n (n x k)
+    const int64_t a_row = pb.trans_a ? a->m : a->k;
+    const int64_t b_row = pb.trans_b ? a->k : a->n;
+    pb.lda = a->lda ? a->lda : a_row;
+    pb.ldb = a->ldb ? a->ldb : b_row;
     pb.ldc = a->ldc ? a->ldc : a->n;
     pb.stream = static_cast<cudaStream_t>(a->stream);
     pb.tile_n = a->tile_n;
-    if (pb.lda < pb.k || pb.ldb < pb.n || pb.ldc < pb.n || pb.lda < 0 || pb.ldb < 0 || pb.ldc < 0)
-        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: leading dimension smaller than the row length");
+    if (pb.lda < a_row || pb.ldb < b_row || pb.ldc < pb.n || pb.lda < 0 || pb.ldb < 0 || pb.ldc < 0)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "%s: leading dimension smaller than the row length", name);
+    if (x != nullptr) {
+        pb.ep = (x->alpha != 1.f || x->beta != 0.f || x->bias != nullptr || x->activation != VK_ACT_NONE) ? 1 : 0;
+        pb.act = x->activation;
+        pb.alpha = x->alpha;
+        pb.beta = x->beta;
+        pb.Cin = x->beta != 0.f ? x->C_in : nullptr;
+        pb.ldcin = x->ldc_in ? x->ldc_in : pb.ldc;
+        pb.bias = x->bias;
+        if (pb.Cin != nullptr && pb.ldcin < pb.n)
+            return set_error(VK_ERR_INVALID_ARGUMENT, "%s: ldc_in smaller than n", name);
+    }
     if (a->dtype == VK_DTYPE_F32 && a->acc != VK_ACC_F32)
-        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: fp32 GEMM supports fp32 accumulation only");
+        return set_error(VK_ERR_UNSUPPORTED, "%s: fp32 GEMM supports fp32 accumulation only", name);
     if (a->dtype == VK_DTYPE_F32 && a->C_f32 != nullptr)
-        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: C_f32 copy is for fp16 output only");
+        return set_error(VK_ERR_INVALID_ARGUMENT, "%s: C_f32 copy is for fp16 output only", name);
+    if (a->dtype == VK_DTYPE_F32 && (pb.trans_a || pb.trans_b))
+        return set_error(VK_ERR_UNSUPPORTED, "%s: transposed operands are supported for fp16 only", name);
     if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256)
-        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: tile_n must be 0, 128 or 256");
+        return set_error(VK_ERR_INVALID_ARGUMENT, "%s: tile_n must be 0, 128 or 256", name);
 
     int dev = 0;
     DeviceState* st = nullptr;
@@ -554,6 +623,10 @@ extern "C" int vk_gemm(const vk_gemm_args* a)
     if (rc != VK_OK) return rc;
     return dispatch(*st, dev, pb, a->dtype, a->acc, a->algo);
 }
+
+extern "C" int vk_gemm(const vk_gemm_args* a) { return gemm_entry(a, nullptr, "vk_gemm"); }
+
+extern "C" int vk_gemm_ex(const vk_gemm_args* a, const vk_gemm_ext* x) { return gemm_entry(a, x, "vk_gemm_ex"); }
 
 namespace vk {
 int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc, int algo_in)
