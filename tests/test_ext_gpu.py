@@ -103,7 +103,10 @@ def test_fused_epilogue_fp16(vk, algo, tile_n, shape, opts):
     c32 = C32.cpu().numpy()
     assert v0.rel_frobenius(c32, ref) <= FROB
     assert v0.max_elem_rel(c32, ref) <= ELEM
-    assert v0.max_elem_rel(C.cpu().numpy(), ref.astype(np.float16)) <= ELEM
+    # The fp16 output is compared with one more fp16 ulp (2^-10) of slack: after cancellation
+    # (alpha * A@B and bias of opposite sign) the GEMM's fp32 summation error plus two independent
+    # roundings to fp16 can reach two ulps of a small result; the fp32 copy above keeps the 2e-3 bound.
+    assert v0.max_elem_rel(C.cpu().numpy(), ref.astype(np.float16)) <= ELEM + 2.0 ** -10
 
 
 @pytest.mark.parametrize("shape", [(1000, 1000, 1000), (300, 200, 20), (130, 131, 17)])
