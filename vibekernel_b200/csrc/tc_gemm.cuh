@@ -37,6 +37,8 @@
 
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "ptx.cuh"
 
 namespace vk {
@@ -365,13 +367,17 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
-        if (rank == 0 && lane == 0) {
+        // One copy of the issue loop per operand layout, so the descriptor arithmetic of the
+        // single issuing thread is resolved at compile time (its issue rate matters).
+        auto mma_loop = [&](auto a_mn_tag, auto b_k_tag) {
+            constexpr bool A_MN = decltype(a_mn_tag)::value;
+            constexpr bool B_K = decltype(b_k_tag)::value;
             // M/N-major operands: 64-element atoms of BK rows x 128 B, LBO steps between atoms and
-            // SBO between 8-row groups, k advances 16 rows (2 KB) per MMA.  K-major operands: rows of
-            // 128 B in 8-row groups (SBO), k advances 32 B within a 64-wide span and a whole span
+            // SBO between 8-row groups, k advances 16 rows (2 KB) per MMA.  K-major operands: rows
+            // of 128 B in 8-row groups (SBO), k advances 32 B within a 64-wide span and a whole span
             // (box) every 4 MMAs.
-            const uint32_t idesc = idesc_f16(BM * CG, BN, ACC_F32, /*b_mn_major=*/!p.b_k) |
-                                   (p.a_mn ? (1u << 15) : 0u);
+            constexpr uint32_t kIdesc =
+                idesc_f16(BM * CG, BN, ACC_F32, /*b_mn_major=*/!B_K) | (A_MN ? (1u << 15) : 0u);
             constexpr uint32_t kMnLbo = Cfg::kBK * 128;
             int stage = 0;
             uint32_t phase = 0;
@@ -396,12 +402,12 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                     for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
                         const uint64_t a_desc =
-                            p.a_mn ? smem_desc_sw128(a_addr + kk * 16 * 128, kMnLbo, 1024)
-                                   : smem_desc_sw128(a_addr + (kk >> 2) * Cfg::kABox + (kk & 3) * 32, 16, 1024);
+                            A_MN ? smem_desc_sw128(a_addr + kk * 16 * 128, kMnLbo, 1024)
+                                 : smem_desc_sw128(a_addr + (kk >> 2) * Cfg::kABox + (kk & 3) * 32, 16, 1024);
                         const uint64_t b_desc =
-                            p.b_k ? smem_desc_sw128(b_addr + (kk >> 2) * Cfg::kBKBox + (kk & 3) * 32, 16, 1024)
-                                  : smem_desc_sw128(b_addr + kk * 16 * 128, kMnLbo, 1024);
-                        umma_f16<CG>(d_tmem, a_desc, b_desc, idesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
+                            B_K ? smem_desc_sw128(b_addr + (kk >> 2) * Cfg::kBKBox + (kk & 3) * 32, 16, 1024)
+                                : smem_desc_sw128(b_addr + kk * 16 * 128, kMnLbo, 1024);
+                        umma_f16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
                     }
                     const uint32_t eb = empty_bar(stage);
                     umma_commit<CG>(eb);
@@ -417,6 +423,18 @@ __global__ void __launch_bounds__(192, 1)
                 if constexpr (CG == 2) umma_commit<CG>(mapa_shared(tb, 1));
                 trace_at(p.trace, 4);
             }
+        };
+        if (rank == 0 && lane == 0) {
+            using T = std::true_type;
+            using F = std::false_type;
+            if (!p.a_mn && !p.b_k)
+                mma_loop(F{}, F{});
+            else if (!p.a_mn)
+                mma_loop(F{}, T{});
+            else if (!p.b_k)
+                mma_loop(T{}, F{});
+            else
+                mma_loop(T{}, T{});
         }
     } else {
         // ------------------------------------------------------------------ epilogue
