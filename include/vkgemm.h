@@ -184,7 +184,10 @@ int vk_selftest_wait_timeout(int device, int64_t timeout_us);
 int vk_set_wait_timeout_ns(uint64_t ns);
 
 /* Process-wide tuning knobs (no counterpart in the reference, whose versions hard-code them):
- *   "tail_split"      1 (default) = cut the tiles of a partial last wave into k-slices, 0 = off
+ *   "tail_split"      1 (default) = cut the tiles of a partial last wave (into column halves or
+ *                     k-slices, see "tail_nsplit"), 0 = off
+ *   "tail_nsplit"     1 (default) = prefer column halves for the last wave when it is at most half
+ *                     full; 0 = k-slices only
  *   "raster_group"    tiles along M per rasterisation group of the persistent scheduler (8)
  *   "bk_2sm256"       k per pipeline stage of the 256-column pair kernel: 128 (default, 3 stages
  *                     of 64 KB) or 64 (6 stages of 32 KB)
@@ -209,6 +212,12 @@ int vk_read_clock_probe(int device, uint64_t* out3, int clear);
  * CTA entry, [10]/[11] earliest/latest CTA exit.  Read once, re-arm for the next launch first
  * (call it once before tracing).  Synchronises. */
 int vk_read_trace(int device, uint64_t* out16);
+
+/* Per-CTA part of the same timeline (no counterpart in the reference): for the first max_ctas CTAs
+ * (at most 256), eight words each: entry, last MMA commit (pair leaders / single CTAs), last epilogue
+ * store, exit (%globaltimer ns), SM id, units processed, last accumulator ready at the epilogue,
+ * k-sliced tail: partial published / all other partials published.  Synchronises. */
+int vk_read_trace_cta(int device, uint64_t* out, int max_ctas);
 
 #ifdef __cplusplus
 }

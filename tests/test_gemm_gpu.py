@@ -232,6 +232,32 @@ def test_repeated_launches_are_bitwise_identical(vk, shape, acc):
     assert v0.rel_frobenius(first.cpu().numpy().astype(np.float32), g32) <= max(tol, 5e-4)
 
 
+@pytest.mark.parametrize("mode", [{"tail_split": 0}, {"tail_nsplit": 0}, {"tail_nsplit": 1}],
+                         ids=["none", "ksplit", "nsplit"])
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (4000, 5120, 3000), (1024, 1024, 1024), (512, 768, 2048),
+                                   (4096, 4096, 1024)])
+@pytest.mark.parametrize("acc", ["f32", "f16"])
+def test_tail_modes(vk, mode, shape, acc):
+    """Whole-tile, k-sliced and column-halved last waves all agree with the oracle."""
+    m, n, k = shape
+    A, B = v0.make_inputs(m, n, k, 57, lo=-0.5, hi=0.5)
+    try:
+        for name, val in mode.items():
+            vk.set_option(name, val)
+        c16, c32 = _run16(vk, A, B, acc=acc)
+        again, _ = _run16(vk, A, B, acc=acc)
+    finally:
+        vk.set_option("tail_split", 1)
+        vk.set_option("tail_nsplit", 1)
+    assert np.array_equal(c16.view(np.uint16), again.view(np.uint16))
+    g32 = v0.v0_f16(A, B)[1]
+    if acc == "f32":
+        assert v0.rel_frobenius(c32, g32) <= FROB_F32ACC
+        assert v0.max_elem_rel(c32, g32) <= ELEM
+    else:
+        assert v0.rel_frobenius(c16.astype(np.float32), g32) <= FROB_F16ACC
+
+
 def test_split_gemms_on_concurrent_streams(vk):
     """Two k-sliced GEMMs in flight on different streams must not share tail-split scratch."""
     A1, B1 = v0.make_inputs(1024, 1024, 2048, 55)

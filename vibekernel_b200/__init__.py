@@ -39,7 +39,7 @@ EXPORTED = (
     "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
     "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
-    "vk_gemm_host", "vk_gemm_ex",
+    "vk_gemm_host", "vk_gemm_ex", "vk_read_trace_cta",
 )
 
 
@@ -121,6 +121,8 @@ def _load() -> ctypes.CDLL:
     lib.vk_read_clock_probe.restype = ctypes.c_int
     lib.vk_read_trace.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint64)]
     lib.vk_read_trace.restype = ctypes.c_int
+    lib.vk_read_trace_cta.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]
+    lib.vk_read_trace_cta.restype = ctypes.c_int
     return lib
 
 
@@ -304,6 +306,20 @@ def read_trace(device: int = 0) -> dict:
     v = [int(x) for x in out]
     t0 = v[8]
     return {name: (v[i] - t0) / 1e3 for i, name in enumerate(TRACE_FIELDS)}
+
+
+def read_trace_cta(device: int = 0, ctas: int = 148):
+    """Per-CTA timeline of the last traced launch: list of dicts (times in us from earliest entry)."""
+    out = (ctypes.c_uint64 * (8 * ctas))()
+    check(lib.vk_read_trace_cta(device, out, ctas))
+    rows = [[int(out[8 * i + j]) for j in range(8)] for i in range(ctas)]
+    t0 = min(r[0] for r in rows if r[0])
+
+    def rel(v):
+        return (v - t0) / 1e3 if v else None
+    return [{"cta": i, "entry": rel(r[0]), "last_commit": rel(r[1]), "last_store": rel(r[2]), "exit": rel(r[3]),
+             "smid": r[4], "units": r[5], "last_acc_ready": rel(r[6]), "tail_sync": rel(r[7])}
+            for i, r in enumerate(rows)]
 
 
 def set_wait_timeout_ns(ns: int) -> None:

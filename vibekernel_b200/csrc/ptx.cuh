@@ -40,6 +40,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns()
 // [7] CTA 0 exit, [8] earliest CTA entry, [9] latest CTA entry, [10] earliest CTA exit,
 // [11] latest CTA exit.
 __device__ unsigned long long g_trace[16];
+// Per-CTA timeline (trace option): for CTA b < 256, [b][0] entry, [b][1] last MMA commit (pair leader
+// or single CTA), [b][2] last epilogue store, [b][3] exit, [b][4] SM id, [b][5] units processed,
+// [b][6] last accumulator ready at the epilogue, [b][7] tail slice: partial published / others'
+// partials all published (last arriver).
+__device__ unsigned long long g_trace_cta[256][8];
 
 __device__ __forceinline__ void trace_at(int trace, int slot)
 {
@@ -190,6 +195,38 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
         : "memory");
+}
+
+// Orders this thread's generic-proxy global-memory accesses (and what it acquired) before later
+// async-proxy ones (bulk copies reading global memory).
+__device__ __forceinline__ void fence_proxy_async_global()
+{
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bounded wait until the counter at `addr` (global) reaches at least `target`, with acquire
+// semantics; records (code, detail) and returns false when `timeout_ns` passes or another wait
+// has already given up.
+__device__ __forceinline__ bool wait_count_at_least(int* addr, int target, uint64_t timeout_ns, uint32_t code,
+                                                    uint32_t detail)
+{
+    auto load = [&]() {
+        int v;
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+        return v;
+    };
+    if (load() >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 32; ++i)
+            if (load() >= target) return true;
+        if (device_error_set()) return false;
+        if (globaltimer_ns() - t0 > timeout_ns) {
+            record_error(code, detail);
+            return false;
+        }
+    }
 }
 
 // Orders this thread's generic-proxy shared-memory accesses before later async-proxy ones.

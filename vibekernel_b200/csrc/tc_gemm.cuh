@@ -52,11 +52,11 @@ struct TcParams {
     float* C32;              // optional fp32 copy, ld = N
     int vec_ok;              // C / C32 alignment allows 16-byte stores
     unsigned long long timeout_ns;
-    // work units: [0, full_units) are whole tiles, then (units - full_units) / split tail tiles
-    // cut into `split` k-slices each
-    int units, full_units, split;
+    // work units: [0, full_units) are whole tiles; then the tail tiles, each cut either into two
+    // column halves (nsplit = 1: BN/2-wide MMAs, no reduction) or into `split` k-slices
+    int units, full_units, split, nsplit;
     float* ws;               // split partials: [tail tile][slice][CTA rank][128 rows x BN] fp32
-    int* counters;           // arrival counters: [tail tile][CTA rank][4 epilogue warps]
+    int* counters;           // [tail tile][CTA rank][4 epilogue warps][arrived, published]
     int clock_probe;         // 1: CTA 0 accumulates (cycles, ns, launches) into g_clock_probe
     int trace;               // 1: record the launch timeline into g_trace
     // operand layouts: a_mn = A stored k x m (A^T row-major: M-major tiles); b_k = B stored n x k
@@ -70,34 +70,26 @@ struct TcParams {
     const __half* bias;
 };
 
-// Fused epilogue for one row's 32 fp32 results at columns col .. col+31 (fp32 math, then round).
-__device__ __forceinline__ void store_chunk_fused(const TcParams& p, int row, int col, float (&f)[32])
-{
-    if (row >= p.M) return;
-    __half* crow = p.C + static_cast<long long>(row) * p.ldc;
-    const __half* cin = p.Cin ? p.Cin + static_cast<long long>(row) * p.ldcin : nullptr;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        if (col + i < p.N) {
-            float v = p.alpha * f[i];
-            if (cin != nullptr && p.beta != 0.f) v = fmaf(p.beta, __half2float(cin[col + i]), v);
-            if (p.bias != nullptr) v += __half2float(p.bias[col + i]);
-            if (p.act == 1) v = fmaxf(v, 0.f);
-            crow[col + i] = __float2half_rn(v);
-            if (p.C32 != nullptr) p.C32[static_cast<long long>(row) * p.N + col + i] = v;
-        }
-    }
-}
 
 struct Unit {
-    int tile, kb0, kb1, slice;  // slice < 0: whole tile
+    int tile, kb0, kb1;
+    int slice;  // k-slice index of a k-split tail tile, -1 otherwise
+    int half;   // column half (0/1) of an n-split tail tile, -1 for the full width
 };
 
 __device__ __forceinline__ Unit unit_info(const TcParams& p, int u)
 {
     Unit w;
+    w.half = -1;
     if (u < p.full_units) {
         w.tile = u;
+        w.kb0 = 0;
+        w.kb1 = p.num_kb;
+        w.slice = -1;
+    } else if (p.nsplit) {
+        const int v = u - p.full_units;
+        w.tile = p.full_units + (v >> 1);
+        w.half = v & 1;
         w.kb0 = 0;
         w.kb1 = p.num_kb;
         w.slice = -1;
@@ -111,6 +103,10 @@ __device__ __forceinline__ Unit unit_info(const TcParams& p, int u)
     }
     return w;
 }
+
+// Bytes of the per-warp staging buffer of the epilogue: 32 rows x 32 fp16 = 64 B, pitch 80 B.
+constexpr int kEpiPitch = 80;
+constexpr int kEpiWarpBytes = 32 * kEpiPitch;
 
 template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
 struct TcCfg {
@@ -131,7 +127,8 @@ struct TcCfg {
     // The tail-split reduction stages other slices' partials in the (idle) pipeline buffers:
     // 48 KB per epilogue warp.
     static constexpr int kRedFloatsPerWarp = 12288;
-    static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kNumBars * 8 + 16;
+    static constexpr int kSmemBytes =
+        1024 /*alignment slack*/ + STAGES * kStageBytes + kNumBars * 8 + 32 + 4 * kEpiWarpBytes;
     static constexpr int kThreads = 192;
     static_assert(CG == 1 || CG == 2, "cta group");
     static_assert(KA == 1 || KA == 2, "k spans per stage");
@@ -159,79 +156,78 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Store one row's 32 consecutive results (r = raw TMEM words) at C[row, col .. col+31].
+// TMEM words of one 32-column chunk to fp32 values (fp16 accumulators sit in the low halves).
 template <bool ACC_F32>
-__device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col, const uint32_t (&r)[32])
+__device__ __forceinline__ void tmem_words_to_f32(const uint32_t (&r)[32], float (&f)[32])
 {
-    if (row >= p.M) return;
-    if (p.ep) {
-        float f[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            if constexpr (ACC_F32)
-                f[i] = __uint_as_float(r[i]);
-            else
-                f[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(r[i])));
-        }
-        store_chunk_fused(p, row, col, f);
-        return;
+    for (int i = 0; i < 32; ++i) {
+        if constexpr (ACC_F32)
+            f[i] = __uint_as_float(r[i]);
+        else
+            f[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(r[i])));
     }
-    __half* crow = p.C + static_cast<long long>(row) * p.ldc;
-    const bool full = (col + 32 <= p.N) && p.vec_ok;
-    if (full) {
-        uint4* dst = reinterpret_cast<uint4*>(crow + col);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint4 v;
-            if constexpr (ACC_F32) {
-                v.x = pack_half2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
-                v.y = pack_half2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
-                v.z = pack_half2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
-                v.w = pack_half2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
-            } else {
-                // fp16 accumulators occupy the low 16 bits of each 32-bit TMEM column.
-                v.x = __byte_perm(r[8 * j + 0], r[8 * j + 1], 0x5410);
-                v.y = __byte_perm(r[8 * j + 2], r[8 * j + 3], 0x5410);
-                v.z = __byte_perm(r[8 * j + 4], r[8 * j + 5], 0x5410);
-                v.w = __byte_perm(r[8 * j + 6], r[8 * j + 7], 0x5410);
-            }
-            dst[j] = v;
-        }
-        if (p.C32 != nullptr) {
-            float4* d32 = reinterpret_cast<float4*>(p.C32 + static_cast<long long>(row) * p.N + col);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                float4 f;
-                if constexpr (ACC_F32) {
-                    f = make_float4(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1]),
-                                    __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-                } else {
-                    f = make_float4(__half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 0]))),
-                                    __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 1]))),
-                                    __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 2]))),
-                                    __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 3]))));
-                }
-                d32[j] = f;
-            }
-        }
-    } else {
+}
+
+// One warp writes its 32 rows x 32 columns of C (this lane's row = row0 + lane, values f for
+// columns col .. col+31): the fused epilogue and the fp32 copy are applied per row, then the fp16
+// results go through the warp's staging buffer so that each global store instruction writes 64-byte
+// runs of 8 rows (4 lanes per row) instead of 16 bytes of 32 different rows.
+__device__ __forceinline__ void store_rows(const TcParams& p, uint8_t* stg, int row0, int lane, int col,
+                                           float (&f)[32])
+{
+    const int row = row0 + lane;
+    if (p.ep && row < p.M) {
+        const __half* cin = p.Cin ? p.Cin + static_cast<long long>(row) * p.ldcin : nullptr;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
             if (col + i < p.N) {
-                float f;
-                __half h;
-                if constexpr (ACC_F32) {
-                    f = __uint_as_float(r[i]);
-                    h = __float2half_rn(f);
-                } else {
-                    h = __ushort_as_half(static_cast<unsigned short>(r[i]));
-                    f = __half2float(h);
-                }
-                crow[col + i] = h;
-                if (p.C32 != nullptr) p.C32[static_cast<long long>(row) * p.N + col + i] = f;
+                float v = p.alpha * f[i];
+                if (cin != nullptr && p.beta != 0.f) v = fmaf(p.beta, __half2float(cin[col + i]), v);
+                if (p.bias != nullptr) v += __half2float(p.bias[col + i]);
+                if (p.act == 1) v = fmaxf(v, 0.f);
+                f[i] = v;
             }
         }
     }
+    if (p.C32 != nullptr && row < p.M) {
+        float* d32 = p.C32 + static_cast<long long>(row) * p.N + col;
+        if (col + 32 <= p.N && p.vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                reinterpret_cast<float4*>(d32)[j] = make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (col + i < p.N) d32[i] = f[i];
+        }
+    }
+    uint4* srow = reinterpret_cast<uint4*>(stg + lane * kEpiPitch);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        srow[j] = make_uint4(pack_half2(f[8 * j], f[8 * j + 1]), pack_half2(f[8 * j + 2], f[8 * j + 3]),
+                             pack_half2(f[8 * j + 4], f[8 * j + 5]), pack_half2(f[8 * j + 6], f[8 * j + 7]));
+    __syncwarp();
+    const int seg = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int rr = (lane >> 2) + 8 * j;
+        const int grow = row0 + rr;
+        const int gcol = col + seg * 8;
+        if (grow < p.M && gcol < p.N) {
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * kEpiPitch + seg * 16);
+            __half* dst = p.C + static_cast<long long>(grow) * p.ldc + gcol;
+            if (gcol + 8 <= p.N && p.vec_ok) {
+                *reinterpret_cast<uint4*>(dst) = v;
+            } else {
+                const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    if (gcol + e < p.N) dst[e] = h[e];
+            }
+        }
+    }
+    __syncwarp();
 }
 
 template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
@@ -248,6 +244,7 @@ __global__ void __launch_bounds__(192, 1)
     uint8_t* sB = smem + STAGES * Cfg::kABytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kBBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+    uint8_t* epi_stage = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_slot) + 4 + 15) & ~uintptr_t(15));
 
     const uint32_t bar0 = smem_u32(bars);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -263,6 +260,12 @@ __global__ void __launch_bounds__(192, 1)
         if (blockIdx.x == 0) g_trace[0] = t;
         atomicMin(&g_trace[8], t);
         atomicMax(&g_trace[9], t);
+        if (blockIdx.x < 256) {
+            unsigned int smid;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+            g_trace_cta[blockIdx.x][0] = t;
+            g_trace_cta[blockIdx.x][4] = smid;
+        }
     }
     const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
     const int cluster_id = blockIdx.x / CG;
@@ -310,7 +313,10 @@ __global__ void __launch_bounds__(192, 1)
                 int tm, tn;
                 tile_coords(w.tile, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
                 const int m0 = tm * (BM * CG) + static_cast<int>(rank) * BM;
-                const int n0 = tn * BN + static_cast<int>(rank) * Cfg::kBNCta;
+                // an n-split half tile: BN/2 columns, BN/2/CG per CTA (whole 64-column boxes)
+                const int bn_cta = w.half >= 0 ? Cfg::kBNCta / 2 : Cfg::kBNCta;
+                const int n0 = tn * BN + (w.half > 0 ? BN / 2 : 0) + static_cast<int>(rank) * bn_cta;
+                const uint32_t stage_bytes = Cfg::kABytes + static_cast<uint32_t>(bn_cta) * Cfg::kBK * 2;
                 for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, kErrWaitProducer, stage)) {
                         ok = false;
@@ -322,9 +328,9 @@ __global__ void __launch_bounds__(192, 1)
                     const int k0 = kb * Cfg::kBK;
                     uint32_t bar = fb;
                     if constexpr (CG == 1) {
-                        mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+                        mbar_arrive_expect_tx(fb, stage_bytes);
                     } else {
-                        if (rank == 0) mbar_arrive_expect_tx(fb, 2 * Cfg::kStageBytes);
+                        if (rank == 0) mbar_arrive_expect_tx(fb, 2 * stage_bytes);
                         bar = mapa_shared(fb, 0);
                     }
                     auto load = [&](uint32_t dst, const CUtensorMap* map, int c0, int c1) {
@@ -342,7 +348,8 @@ __global__ void __launch_bounds__(192, 1)
                     }
                     if (!p.b_k) {
 #pragma unroll
-                        for (int j = 0; j < Cfg::kBBoxes; ++j) load(b_dst + j * Cfg::kBBox, &tmap_b, n0 + 64 * j, k0);
+                        for (int j = 0; j < Cfg::kBBoxes; ++j)
+                            if (j * 64 < bn_cta) load(b_dst + j * Cfg::kBBox, &tmap_b, n0 + 64 * j, k0);
                     } else {
 #pragma unroll
                         for (int a = 0; a < KA; ++a) load(b_dst + a * Cfg::kBKBox, &tmap_b, k0 + 64 * a, n0);
@@ -378,6 +385,8 @@ __global__ void __launch_bounds__(192, 1)
             // (box) every 4 MMAs.
             constexpr uint32_t kIdesc =
                 idesc_f16(BM * CG, BN, ACC_F32, /*b_mn_major=*/!B_K) | (A_MN ? (1u << 15) : 0u);
+            constexpr uint32_t kIdescHalf =
+                idesc_f16(BM * CG, BN / 2, ACC_F32, /*b_mn_major=*/!B_K) | (A_MN ? (1u << 15) : 0u);
             constexpr uint32_t kMnLbo = Cfg::kBK * 128;
             int stage = 0;
             uint32_t phase = 0;
@@ -390,6 +399,7 @@ __global__ void __launch_bounds__(192, 1)
                 if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, kErrWaitMma, 100 + acc)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                const uint32_t idesc = w.half >= 0 ? kIdescHalf : kIdesc;
                 for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, kErrWaitMma, stage)) {
                         ok = false;
@@ -407,7 +417,7 @@ __global__ void __launch_bounds__(192, 1)
                         const uint64_t b_desc =
                             B_K ? smem_desc_sw128(b_addr + (kk >> 2) * Cfg::kBKBox + (kk & 3) * 32, 16, 1024)
                                 : smem_desc_sw128(b_addr + kk * 16 * 128, kMnLbo, 1024);
-                        umma_f16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
+                        umma_f16<CG>(d_tmem, a_desc, b_desc, idesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
                     }
                     const uint32_t eb = empty_bar(stage);
                     umma_commit<CG>(eb);
@@ -422,6 +432,10 @@ __global__ void __launch_bounds__(192, 1)
                 umma_commit<CG>(tb);
                 if constexpr (CG == 2) umma_commit<CG>(mapa_shared(tb, 1));
                 trace_at(p.trace, 4);
+                if (p.trace && blockIdx.x < 256) {
+                    g_trace_cta[blockIdx.x][1] = globaltimer_ns();
+                    g_trace_cta[blockIdx.x][5] = static_cast<unsigned long long>(it + 1);
+                }
             }
         };
         if (rank == 0 && lane == 0) {
@@ -446,142 +460,146 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
             if (!mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, kErrWaitEpilogue, acc)) break;
             if (it == 0 && warp == 2 && lane == 0) trace_at(p.trace, 5);
+            if (p.trace && warp == 2 && lane == 0 && blockIdx.x < 256) g_trace_cta[blockIdx.x][6] = globaltimer_ns();
             tc_fence_after();
             int tm, tn;
             tile_coords(w.tile, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
-            const int row = tm * (BM * CG) + static_cast<int>(rank) * BM + q * 32 + lane;
-            const int col0 = tn * BN;
+            const int row0 = tm * (BM * CG) + static_cast<int>(rank) * BM + q * 32;  // this warp's rows
+            uint8_t* stg = epi_stage + q * kEpiWarpBytes;
+            const int col0 = tn * BN + (w.half > 0 ? BN / 2 : 0);
+            const int bn_eff = w.half >= 0 ? BN / 2 : BN;  // columns of this unit
             const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
             if (w.slice >= 0) {
-                // Tail slice: publish this slice's fp32 partial (lane-major float4 runs, so each warp
-                // store is one contiguous 512-byte span), then count arrivals; only the last slice
-                // to arrive reduces and writes C.
+                // Tail slice.  Arrivals are counted first: every slice but the last to arrive publishes
+                // its fp32 partial (lane-major float4 runs: each warp store is one contiguous 512-byte
+                // span) and then counts itself as published; the last one waits (bounded) until the
+                // others have published, adds them to its own accumulator in slice order and writes C.
                 const int ti = w.tile - p.full_units;
                 constexpr size_t kRegion = static_cast<size_t>(BM) * BN;
                 const size_t warp_off = static_cast<size_t>(q) * 32 * BN;
-                float* mine = p.ws + (static_cast<size_t>(ti * p.split + w.slice) * CG + rank) * kRegion + warp_off;
-#pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
-                    tmem_ld_wait();
-                    float4* dst = reinterpret_cast<float4*>(mine + c * 32);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        float4 f;
-                        if constexpr (ACC_F32) {
-                            f = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-                        } else {
-                            f = make_float4(__half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j]))),
-                                            __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 1]))),
-                                            __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 2]))),
-                                            __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * j + 3]))));
-                        }
-                        __stcg(dst + j * 32 + lane, f);
-                    }
-                }
-                __threadfence();
-                __syncwarp();
-                int* ctr = p.counters + (ti * CG + static_cast<int>(rank)) * 4 + q;
+                int* ctr = p.counters + ((ti * CG + static_cast<int>(rank)) * 4 + q) * 2;  // arrived, published
                 int old = 0;
-                if (lane == 0) old = atomicAdd(ctr, 1);
+                if (lane == 0) old = atomicAdd(&ctr[0], 1);
                 old = __shfl_sync(0xffffffffu, old, 0);
-                if (old == p.split - 1) {
+                if (old < p.split - 1) {
+                    float* mine = p.ws + (static_cast<size_t>(ti * p.split + w.slice) * CG + rank) * kRegion + warp_off;
+#pragma unroll 1
+                    for (int c = 0; c < BN; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
+                        tmem_ld_wait();
+                        float f[32];
+                        tmem_words_to_f32<ACC_F32>(r, f);
+                        float4* dst = reinterpret_cast<float4*>(mine + c * 32);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            __stcg(dst + j * 32 + lane, make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]));
+                    }
                     __threadfence();
-                    // Columns per round so that the other (split - 1) slices' partials of this warp's
-                    // 32 rows fit its 48 KB of staging: (split - 1) * cr <= 384.
-                    int cr = BN;
-                    while ((p.split - 1) * cr > Cfg::kRedFloatsPerWarp / 32) cr >>= 1;
-                    float* red = reinterpret_cast<float*>(smem) + q * Cfg::kRedFloatsPerWarp;
-                    uint32_t rphase = 0;
+                    __syncwarp();
+                    if (lane == 0) atomicAdd(&ctr[1], 1);
+                    if (p.trace && warp == 2 && lane == 0 && blockIdx.x < 256) g_trace_cta[blockIdx.x][7] = globaltimer_ns();
+                } else {
+                    bool ok = true;
+                    if (lane == 0) ok = wait_count_at_least(&ctr[1], p.split - 1, p.timeout_ns, kErrWaitEpilogue, 300 + q);
+                    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                    if (p.trace && warp == 2 && lane == 0 && blockIdx.x < 256) g_trace_cta[blockIdx.x][7] = globaltimer_ns();
+                    if (ok) {
+                        __threadfence();
+                        if (lane == 0) fence_proxy_async_global();  // published partials precede the bulk reads
+                        // Columns per round so that the other (split - 1) slices' partials of this warp's
+                        // 32 rows fit its 48 KB of staging: (split - 1) * cr <= 384.
+                        int cr = BN;
+                        while ((p.split - 1) * cr > Cfg::kRedFloatsPerWarp / 32) cr >>= 1;
+                        float* red = reinterpret_cast<float*>(smem) + q * Cfg::kRedFloatsPerWarp;
+                        uint32_t rphase = 0;
 #pragma unroll 1
-                    for (int c0 = 0; c0 < BN && col0 + c0 < p.N; c0 += cr) {
-                        if (lane == 0) {
-                            fence_proxy_async_smem();  // earlier reads of `red` precede the refill
-                            mbar_arrive_expect_tx(red_bar(q), static_cast<uint32_t>((p.split - 1) * cr * 32 * 4));
-                            int j = 0;
-                            for (int s2 = 0; s2 < p.split; ++s2) {
-                                if (s2 == w.slice) continue;
-                                const float* src = p.ws + (static_cast<size_t>(ti * p.split + s2) * CG + rank) * kRegion +
-                                                   warp_off + static_cast<size_t>(c0) * 32;
-                                bulk_load(smem_u32(red + j * cr * 32), src, static_cast<uint32_t>(cr * 32 * 4), red_bar(q));
-                                ++j;
-                            }
-                        }
-                        if (!mbar_wait(red_bar(q), rphase, p.timeout_ns, kErrWaitEpilogue, 200 + q)) break;
-                        rphase ^= 1u;
-#pragma unroll 1
-                        for (int c = c0; c < c0 + cr; c += 32) {
-                            if (col0 + c >= p.N) break;
-                            uint32_t r[32];
-                            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
-                            tmem_ld_wait();
-                            // f = ((p_0 + p_1) + p_2) + ... in slice order, p_own taken from TMEM
-                            float f[32];
-                            int j = 0;
-#pragma unroll 1
-                            for (int s2 = 0; s2 < p.split; ++s2) {
-                                float4 v[8];
-                                if (s2 == w.slice) {
-#pragma unroll
-                                    for (int jj = 0; jj < 8; ++jj) {
-                                        if constexpr (ACC_F32) {
-                                            v[jj] = make_float4(__uint_as_float(r[4 * jj]), __uint_as_float(r[4 * jj + 1]),
-                                                                __uint_as_float(r[4 * jj + 2]), __uint_as_float(r[4 * jj + 3]));
-                                        } else {
-                                            v[jj] = make_float4(
-                                                __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * jj]))),
-                                                __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * jj + 1]))),
-                                                __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * jj + 2]))),
-                                                __half2float(__ushort_as_half(static_cast<unsigned short>(r[4 * jj + 3]))));
-                                        }
-                                    }
-                                } else {
-                                    const float4* src = reinterpret_cast<const float4*>(red + j * cr * 32 + (c - c0) * 32);
-#pragma unroll
-                                    for (int jj = 0; jj < 8; ++jj) v[jj] = src[jj * 32 + lane];
+                        for (int c0 = 0; c0 < BN && col0 + c0 < p.N; c0 += cr) {
+                            if (lane == 0) {
+                                fence_proxy_async_smem();  // earlier reads of `red` precede the refill
+                                mbar_arrive_expect_tx(red_bar(q), static_cast<uint32_t>((p.split - 1) * cr * 32 * 4));
+                                int j = 0;
+                                for (int s2 = 0; s2 < p.split; ++s2) {
+                                    if (s2 == w.slice) continue;
+                                    const float* src = p.ws + (static_cast<size_t>(ti * p.split + s2) * CG + rank) * kRegion +
+                                                       warp_off + static_cast<size_t>(c0) * 32;
+                                    bulk_load(smem_u32(red + j * cr * 32), src, static_cast<uint32_t>(cr * 32 * 4), red_bar(q));
                                     ++j;
                                 }
-                                if (s2 == 0) {
+                            }
+                            if (!mbar_wait(red_bar(q), rphase, p.timeout_ns, kErrWaitEpilogue, 200 + q)) break;
+                            rphase ^= 1u;
+#pragma unroll 1
+                            for (int c = c0; c < c0 + cr; c += 32) {
+                                if (col0 + c >= p.N) break;
+                                uint32_t r[32];
+                                tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
+                                tmem_ld_wait();
+                                float own[32];
+                                tmem_words_to_f32<ACC_F32>(r, own);
+                                // f = ((p_0 + p_1) + p_2) + ... in slice order, p_own taken from TMEM
+                                float f[32];
+                                int j = 0;
+#pragma unroll 1
+                                for (int s2 = 0; s2 < p.split; ++s2) {
+                                    float4 v[8];
+                                    if (s2 == w.slice) {
 #pragma unroll
-                                    for (int jj = 0; jj < 8; ++jj) {
-                                        f[4 * jj] = v[jj].x;
-                                        f[4 * jj + 1] = v[jj].y;
-                                        f[4 * jj + 2] = v[jj].z;
-                                        f[4 * jj + 3] = v[jj].w;
+                                        for (int jj = 0; jj < 8; ++jj)
+                                            v[jj] = make_float4(own[4 * jj], own[4 * jj + 1], own[4 * jj + 2], own[4 * jj + 3]);
+                                    } else {
+                                        const float4* src = reinterpret_cast<const float4*>(red + j * cr * 32 + (c - c0) * 32);
+#pragma unroll
+                                        for (int jj = 0; jj < 8; ++jj) v[jj] = src[jj * 32 + lane];
+                                        ++j;
                                     }
-                                } else {
+                                    if (s2 == 0) {
 #pragma unroll
-                                    for (int jj = 0; jj < 8; ++jj) {
-                                        f[4 * jj] += v[jj].x;
-                                        f[4 * jj + 1] += v[jj].y;
-                                        f[4 * jj + 2] += v[jj].z;
-                                        f[4 * jj + 3] += v[jj].w;
+                                        for (int jj = 0; jj < 8; ++jj) {
+                                            f[4 * jj] = v[jj].x;
+                                            f[4 * jj + 1] = v[jj].y;
+                                            f[4 * jj + 2] = v[jj].z;
+                                            f[4 * jj + 3] = v[jj].w;
+                                        }
+                                    } else {
+#pragma unroll
+                                        for (int jj = 0; jj < 8; ++jj) {
+                                            f[4 * jj] += v[jj].x;
+                                            f[4 * jj + 1] += v[jj].y;
+                                            f[4 * jj + 2] += v[jj].z;
+                                            f[4 * jj + 3] += v[jj].w;
+                                        }
                                     }
                                 }
+                                store_rows(p, stg, row0, lane, col0 + c, f);
                             }
-                            uint32_t rr[32];
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(f[i]);
-                            store_chunk<true>(p, row, col0 + c, rr);
+                            __syncwarp();
                         }
-                        __syncwarp();
                     }
-                    if (lane == 0) *ctr = 0;  // every slice has arrived: ready for the next launch
+                    if (lane == 0) {  // every slice has arrived and published: ready for the next launch
+                        ctr[0] = 0;
+                        ctr[1] = 0;
+                    }
                 }
             } else {
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = 0; c < bn_eff; c += 32) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
                     tmem_ld_wait();
-                    if (col0 + c < p.N) store_chunk<ACC_F32>(p, row, col0 + c, r);
+                    if (col0 + c < p.N) {
+                        float f[32];
+                        tmem_words_to_f32<ACC_F32>(r, f);
+                        store_rows(p, stg, row0, lane, col0 + c, f);
+                    }
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (warp == 2 && lane == 0) trace_at(p.trace, 6);
+            if (warp == 2 && lane == 0) {
+                trace_at(p.trace, 6);
+                if (p.trace && blockIdx.x < 256) g_trace_cta[blockIdx.x][2] = globaltimer_ns();
+            }
             if (lane == 0) {
                 if constexpr (CG == 1)
                     mbar_arrive(tempty_bar(acc));
@@ -607,6 +625,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     if (p.trace && threadIdx.x == 0) {
         const unsigned long long t = globaltimer_ns();
+        if (blockIdx.x < 256) g_trace_cta[blockIdx.x][3] = t;
         if (blockIdx.x == 0) g_trace[7] = t;
         atomicMin(&g_trace[10], t);
         atomicMax(&g_trace[11], t);

@@ -109,6 +109,7 @@ static std::mutex g_mu;
 static DeviceState g_dev[kMaxDevices];
 static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 static std::atomic<int> g_tail_split{1};
+static std::atomic<int> g_tail_nsplit{1};
 static std::atomic<int> g_raster_group{8};
 // k depth per pipeline stage of the 256-column pair kernel.  Every stage ends with tcgen05.commit
 // to both CTAs' "empty" barriers, and those commits measurably throttle the tensor pipe; 128-deep
@@ -227,7 +228,7 @@ static int ensure_workspace(DeviceState& st, int dev, cudaStream_t stream, float
                          "vk_set_option(\"tail_split\", 0)",
                          DeviceState::kMaxStreams, dev);
     const size_t ws_bytes = static_cast<size_t>(st.sm_count) * 128 * 256 * sizeof(float);
-    const size_t ctr_bytes = static_cast<size_t>(st.sm_count) * 4 * sizeof(int);
+    const size_t ctr_bytes = static_cast<size_t>(st.sm_count) * 4 * 2 * sizeof(int);
     float* ws = nullptr;
     int* ctr = nullptr;
     cudaError_t e = cudaMalloc(&ws, ws_bytes);
@@ -252,18 +253,23 @@ static int ensure_workspace(DeviceState& st, int dev, cudaStream_t stream, float
 // Work decomposition of the persistent tensor-core kernels: whole tiles for the full waves,
 // and the tiles of a partial last wave cut into k-slices (at least kMinSliceKb k-blocks each).
 struct Schedule {
-    int units, full_units, split, grid_units;
+    int units, full_units, split, nsplit, grid_units;
 };
 
 static constexpr int kMinSliceKb = 4;
 static constexpr int kMaxSplit = 8;
 
-static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool allow_split)
+// Tail policy.  With R tail tiles on C clusters: when 2R <= C and the layout allows it, each tail tile
+// is cut into two column halves (MMA N = BN/2, no partial sums), which measured clearly faster than
+// k-slices for the last wave (the k-slice path pays for publishing and reducing fp32 partials); when
+// R <= C/4 the tiles are cut into up to 8 k-slices instead, which parallelises small problems more.
+static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool allow_split, bool allow_nsplit)
 {
     Schedule sc;
     sc.units = static_cast<int>(tiles);
     sc.full_units = static_cast<int>(tiles);
     sc.split = 1;
+    sc.nsplit = 0;
     if (allow_split && tiles > 0) {
         const long long full_waves = tiles / max_units;
         const long long rem = tiles - full_waves * max_units;
@@ -271,7 +277,12 @@ static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool a
             long long s = max_units / rem;
             if (s > num_kb / kMinSliceKb) s = num_kb / kMinSliceKb;
             if (s > kMaxSplit) s = kMaxSplit;
-            if (s >= 2) {
+            const bool ksplit_better = 4 * rem <= max_units && s >= 4;
+            if (allow_nsplit && 2 * rem <= max_units && !ksplit_better) {
+                sc.full_units = static_cast<int>(full_waves * max_units);
+                sc.nsplit = 1;
+                sc.units = static_cast<int>(sc.full_units + 2 * rem);
+            } else if (s >= 2) {
                 sc.full_units = static_cast<int>(full_waves * max_units);
                 sc.split = static_cast<int>(s);
                 sc.units = static_cast<int>(sc.full_units + rem * s);
@@ -370,10 +381,14 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     p.trace = g_trace_on.load(std::memory_order_relaxed);
 
     const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-    const Schedule sc = plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0);
+    // n-split halves need whole 64-column boxes per CTA and N-major B tiles
+    const bool nsplit_ok = (Cfg::kBNCta / 2) % 64 == 0 && !pb.trans_b && g_tail_nsplit.load(std::memory_order_relaxed);
+    const Schedule sc =
+        plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0, nsplit_ok);
     p.units = sc.units;
     p.full_units = sc.full_units;
     p.split = sc.split;
+    p.nsplit = sc.nsplit;
     p.ws = nullptr;
     p.counters = nullptr;
     if (sc.split > 1 && fixed != nullptr) {
@@ -381,7 +396,7 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
         // arrival counters this launch will use (the array keeps the previous call's contents).
         const size_t slots = static_cast<size_t>(sc.units - sc.full_units) * CG;
         const size_t ws_need = slots * Cfg::kBM * BN * sizeof(float);
-        const size_t ctr_need = static_cast<size_t>(sc.units - sc.full_units) / sc.split * CG * 4 * sizeof(int);
+        const size_t ctr_need = static_cast<size_t>(sc.units - sc.full_units) / sc.split * CG * 4 * 2 * sizeof(int);
         if (ws_need > fixed->ws_bytes || ctr_need > fixed->ctr_bytes)
             return set_error(VK_ERR_UNSUPPORTED,
                              "vk_gemm_noalloc: this problem needs %zu bytes of tail-split scratch and %zu bytes "
@@ -817,6 +832,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
         g_tail_split.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
+    if (strcmp(name, "tail_nsplit") == 0) {
+        g_tail_nsplit.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
     if (strcmp(name, "raster_group") == 0) {
         if (value < 1 || value > 64) return set_error(VK_ERR_INVALID_ARGUMENT, "raster_group must be 1..64");
         g_raster_group.store(static_cast<int>(value));
@@ -919,6 +938,20 @@ extern "C" int vk_read_trace(int device, uint64_t* out16)
     cudaSetDevice(prev);
     if (e != cudaSuccess) return cuda_fail(e, "vk_read_trace");
     for (int i = 0; i < 16; ++i) out16[i] = v[i];
+    return VK_OK;
+}
+
+extern "C" int vk_read_trace_cta(int device, uint64_t* out, int max_ctas)
+{
+    if (out == nullptr || max_ctas <= 0) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_read_trace_cta: bad buffer");
+    const int n = max_ctas < 256 ? max_ctas : 256;
+    int prev = 0;
+    VK_CUDA_TRY(cudaGetDevice(&prev));
+    VK_CUDA_TRY(cudaSetDevice(device));
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(out, g_trace_cta, sizeof(uint64_t) * 8 * n);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "vk_read_trace_cta");
     return VK_OK;
 }
 
