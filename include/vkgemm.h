@@ -192,6 +192,9 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *   "bk_2sm256"       k per pipeline stage of the 256-column pair kernel: 128 (default, 3 stages
  *                     of 64 KB) or 64 (6 stages of 32 KB)
  *   "wait_timeout_ns" same as vk_set_wait_timeout_ns
+ *   "repack"          1 (default) = VK_ALGO_AUTO copies an fp16 operand whose pitch or base breaks the
+ *                     TMA rule into a 16-byte-pitched scratch buffer (cached per stream) and runs the
+ *                     tensor-core kernel; 0 = such problems run on the predicated CUDA-core kernel
  *   "sgemm_v2"        1 (default) = fp32 GEMM uses the cp.async pipelined kernel when A and B are
  *                     16-byte aligned with lda, ldb multiples of 4; 0 = always the register-staged one
  *   "clock_probe"     1 = the tensor-core kernels accumulate the SM cycles and nanoseconds of

@@ -131,6 +131,40 @@ def test_unaligned_strides_rejected_by_tc_and_taken_by_auto(vk):
     _check_f32acc(c16, c32, A, B)
 
 
+@pytest.mark.parametrize("shape", [(1000, 999, 1001), (4095, 4097, 4093), (33, 19, 21), (7, 5, 3), (1, 1000, 4001)])
+@pytest.mark.parametrize("repack", [1, 0], ids=["repack", "simt"])
+@pytest.mark.parametrize("layout", [(False, False), (True, True)], ids=["NN", "TT"])
+def test_unaligned_pitch_auto_paths(vk, shape, repack, layout):
+    """Odd K/N (row pitch not a multiple of 16 bytes): AUTO repacks into a pitched buffer for the
+    tensor cores, or (repack off) runs the predicated kernel; both match the oracle."""
+    m, n, k = shape
+    ta, tb = layout
+    A, B = v0.make_inputs(m, n, k, 22)
+    As = np.ascontiguousarray(A.T) if ta else A
+    Bs = np.ascontiguousarray(B.T) if tb else B
+    try:
+        vk.set_option("repack", repack)
+        C32 = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        C = vk.gemm(torch.from_numpy(As).cuda(), torch.from_numpy(Bs).cuda(), trans_a=ta, trans_b=tb, c_f32=C32)
+        torch.cuda.synchronize()
+    finally:
+        vk.set_option("repack", 1)
+    assert vk.device_error(0) == 0
+    _check_f32acc(C.cpu().numpy(), C32.cpu().numpy(), A, B)
+
+
+def test_unaligned_base_pointer_repack(vk):
+    """Views whose first element is not 16-byte aligned (offset by one element)."""
+    A, B = v0.make_inputs(512, 384, 256, 23)
+    Abig = torch.zeros(512 * 256 + 1, dtype=torch.float16, device="cuda")
+    Abig[1:].copy_(torch.from_numpy(A).cuda().reshape(-1))
+    Av = Abig[1:].view(512, 256)
+    C32 = torch.empty((512, 384), dtype=torch.float32, device="cuda")
+    C = vk.gemm(Av, torch.from_numpy(B).cuda(), c_f32=C32)
+    torch.cuda.synchronize()
+    _check_f32acc(C.cpu().numpy(), C32.cpu().numpy(), A, B)
+
+
 def test_sgemm_cfg3_4096_seed3(vk):
     A, B = v0.make_inputs(4096, 4096, 4096, 3, dist="normal", dtype=np.float32)
     C = vk.gemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())

@@ -98,6 +98,9 @@ struct DeviceState {
         cudaStream_t stream = nullptr;
         float* ws = nullptr;
         int* counters = nullptr;
+        // repack buffers for operands whose pitch breaks the TMA rule (grown on demand)
+        void* pack[2] = {nullptr, nullptr};
+        size_t pack_bytes[2] = {0, 0};
     };
     static constexpr int kMaxStreams = 32;
     StreamScratch scratch[kMaxStreams];
@@ -116,6 +119,7 @@ static std::atomic<int> g_raster_group{8};
 // stages (3 x 64 KB) halve them per MMA and beat 64-deep ones (6 x 32 KB) at every size measured.
 static std::atomic<int> g_bk_2sm256{128};
 static std::atomic<int> g_sgemm_v2{1};
+static std::atomic<int> g_repack{1};
 static std::atomic<int> g_clock_probe_on{0};
 static std::atomic<int> g_trace_on{0};
 
@@ -248,6 +252,36 @@ static int ensure_workspace(DeviceState& st, int dev, cudaStream_t stream, float
     *ws_out = ws;
     *ctr_out = ctr;
     return VK_OK;
+}
+
+// Repack buffer `which` (0 = A, 1 = B) of (current device, stream), at least `bytes` long.
+static int ensure_pack(DeviceState& st, int dev, cudaStream_t stream, int which, size_t bytes, void** out)
+{
+    float* ws = nullptr;
+    int* ctr = nullptr;
+    int rc = ensure_workspace(st, dev, stream, &ws, &ctr);  // creates the stream's scratch slot
+    if (rc != VK_OK) return rc;
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (int i = 0; i < st.num_scratch; ++i) {
+        DeviceState::StreamScratch& s = st.scratch[i];
+        if (s.stream != stream) continue;
+        if (s.pack_bytes[which] < bytes) {
+            if (s.pack[which] != nullptr) {
+                // the old buffer may still be read by work queued on this stream
+                cudaError_t e = cudaStreamSynchronize(stream);
+                if (e == cudaSuccess) e = cudaFree(s.pack[which]);
+                if (e != cudaSuccess) return set_error(VK_ERR_CUDA, "repack buffer: %s", cudaGetErrorString(e));
+                s.pack[which] = nullptr;
+                s.pack_bytes[which] = 0;
+            }
+            cudaError_t e = cudaMalloc(&s.pack[which], bytes);
+            if (e != cudaSuccess) return set_error(VK_ERR_CUDA, "repack buffer (%zu bytes): %s", bytes, cudaGetErrorString(e));
+            s.pack_bytes[which] = bytes;
+        }
+        *out = s.pack[which];
+        return VK_OK;
+    }
+    return set_error(VK_ERR_CUDA, "repack buffer: no scratch slot for the stream");
 }
 
 // Work decomposition of the persistent tensor-core kernels: whole tiles for the full waves,
@@ -553,6 +587,8 @@ void release_device_state()
         for (int i = 0; i < st.num_scratch; ++i) {
             cudaFree(st.scratch[i].ws);
             cudaFree(st.scratch[i].counters);
+            for (void* pk : st.scratch[i].pack)
+                if (pk != nullptr) cudaFree(pk);
             st.scratch[i] = DeviceState::StreamScratch();
         }
         st.num_scratch = 0;
@@ -659,9 +695,41 @@ int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc
     }
 
     // fp16
-    const bool tma_ok = tma_ok_f16(pb.A, pb.lda) && tma_ok_f16(pb.B, pb.ldb);
+    const bool a_ok = tma_ok_f16(pb.A, pb.lda), b_ok = tma_ok_f16(pb.B, pb.ldb);
+    const bool tma_ok = a_ok && b_ok;
     int algo = algo_in;
     if (algo == VK_ALGO_FFMA) return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: FFMA kernel is fp32 only");
+    if (algo == VK_ALGO_AUTO && !tma_ok && g_repack.load(std::memory_order_relaxed)) {
+        // Copy the operand(s) that break the TMA rule into a buffer whose row pitch is a multiple of
+        // 16 bytes (one strided device copy each, ordered on the caller's stream), then run the
+        // tensor-core kernel; C keeps its own pitch (the epilogue predicates its stores).
+        Problem pk = pb;
+        for (int which = 0; which < 2; ++which) {
+            if (which == 0 ? a_ok : b_ok) continue;
+            const void* src = which == 0 ? pb.A : pb.B;
+            const int64_t ld = which == 0 ? pb.lda : pb.ldb;
+            const bool trans = which == 0 ? pb.trans_a : pb.trans_b;
+            // stored rows x cols of this operand
+            const int64_t rows = which == 0 ? (trans ? pb.k : pb.m) : (trans ? pb.n : pb.k);
+            const int64_t cols = which == 0 ? (trans ? pb.m : pb.k) : (trans ? pb.k : pb.n);
+            const int64_t ld_new = (cols + 7) / 8 * 8;
+            void* dst = nullptr;
+            int rc2 = ensure_pack(*st, dev, pb.stream, which, static_cast<size_t>(rows) * ld_new * 2, &dst);
+            if (rc2 != VK_OK) return rc2;
+            VK_CUDA_TRY(cudaMemcpy2DAsync(dst, static_cast<size_t>(ld_new) * 2, src, static_cast<size_t>(ld) * 2,
+                                          static_cast<size_t>(cols) * 2, static_cast<size_t>(rows),
+                                          cudaMemcpyDeviceToDevice, pb.stream));
+            if (which == 0) {
+                pk.A = dst;
+                pk.lda = ld_new;
+            } else {
+                pk.B = dst;
+                pk.ldb = ld_new;
+            }
+        }
+        return acc == VK_ACC_F32 ? launch_tc_variant<true>(*st, dev, pk, VK_ALGO_TC_2SM, nullptr)
+                                 : launch_tc_variant<false>(*st, dev, pk, VK_ALGO_TC_2SM, nullptr);
+    }
     if (algo == VK_ALGO_AUTO) algo = tma_ok ? VK_ALGO_TC_2SM : VK_ALGO_SIMT;
     if (algo == VK_ALGO_SIMT) {
         if (acc != VK_ACC_F32)
@@ -844,6 +912,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
     if (strcmp(name, "bk_2sm256") == 0) {
         if (value != 64 && value != 128) return set_error(VK_ERR_INVALID_ARGUMENT, "bk_2sm256 must be 64 or 128");
         g_bk_2sm256.store(static_cast<int>(value));
+        return VK_OK;
+    }
+    if (strcmp(name, "repack") == 0) {
+        g_repack.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
     if (strcmp(name, "sgemm_v2") == 0) {
