@@ -153,6 +153,16 @@ def _stream_handle(stream) -> int | None:
     return int(getattr(stream, "cuda_stream", stream)) or None
 
 
+def _unit_col(t) -> bool:
+    """Unit column stride; a dimension of size 1 may carry any stride."""
+    return t.stride(1) == 1 or t.shape[1] <= 1
+
+
+def _row_pitch(t) -> int:
+    """Row pitch in elements; the stride of a single row does not matter, so use the row length."""
+    return t.stride(0) if t.shape[0] > 1 else max(t.shape[1], 1)
+
+
 def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile_n: int = 0,
          stream=None, lda: int = 0, ldb: int = 0, ldc: int = 0, m: int | None = None,
          n: int | None = None, k: int | None = None, trans_a: bool = False, trans_b: bool = False,
@@ -173,15 +183,15 @@ def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile
     m = (A.shape[1] if trans_a else A.shape[0]) if m is None else m
     k = (A.shape[0] if trans_a else A.shape[1]) if k is None else k
     n = (B.shape[0] if trans_b else B.shape[1]) if n is None else n
-    if A.dim() != 2 or B.dim() != 2 or A.stride(1) != 1 or B.stride(1) != 1:
+    if A.dim() != 2 or B.dim() != 2 or not (_unit_col(A) and _unit_col(B)):
         raise ValueError("A and B must be 2-D with unit column stride")
-    lda = lda or A.stride(0)
-    ldb = ldb or B.stride(0)
+    lda = lda or _row_pitch(A)
+    ldb = ldb or _row_pitch(B)
     if C is None:
         C = torch.empty((m, n), dtype=A.dtype, device=A.device)
-    if C.dim() != 2 or C.stride(1) != 1 or C.dtype != A.dtype:
+    if C.dim() != 2 or not _unit_col(C) or C.dtype != A.dtype:
         raise ValueError("C must be 2-D, unit column stride, same dtype as A")
-    ldc = ldc or C.stride(0)
+    ldc = ldc or _row_pitch(C)
     if c_f32 is not None and (c_f32.dtype != torch.float32 or not c_f32.is_contiguous()):
         raise ValueError("c_f32 must be a contiguous float32 tensor")
     a = GemmArgs()
