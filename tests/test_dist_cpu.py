@@ -52,3 +52,37 @@ def test_two_rank_gloo_sharded_matmul(m):
     for p in procs:
         p.join(timeout=60)
     assert res == {0: True, 1: True}
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 dies before the all-gather; rank 0 must see an error, not hang."""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    A, B = v0.make_inputs(64, 48, 40, 3)
+    off = row_blocks(64, world)
+    C = torch.zeros((64, 48), dtype=torch.float16)
+    if rank == 1:
+        os._exit(3)  # a rank that disappears between steps, without a clean shutdown
+    try:
+        dist_gemm.sharded_matmul(torch.from_numpy(A[off[rank]:off[rank + 1]]), torch.from_numpy(B), C, off, rank,
+                                 _oracle_gemm)
+        q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001 - the error type depends on how gloo notices the loss
+        q.put((rank, "error: " + type(e).__name__))
+
+
+def test_rank_loss_is_detected_not_hung():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, 29577, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    rank0, msg = q.get(timeout=60)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert procs[1].exitcode == 3
+    assert rank0 == 0 and msg.startswith("error"), msg
