@@ -158,7 +158,10 @@ typedef struct vk_shard_args {
     void* const* C;           /* per GPU: full m x n buffer       */
     int64_t m, n, k;
     int32_t dtype, acc, algo; /* as in vk_gemm_args               */
-    int32_t allgather_c;      /* 0 = local row block only          */
+    int32_t allgather_c;      /* 0 = local row block only; 1 = NCCL all-gather after the GEMMs;
+                                 2 = pipelined: each GPU computes its rows in two chunks and pushes
+                                 every finished chunk to all peers with peer-to-peer copies (copy
+                                 engines over NVLink) while the next chunk is computed */
     float* times_ms;          /* optional, length 2: [0] compute max over GPUs, [1] all-gather */
 } vk_shard_args;
 

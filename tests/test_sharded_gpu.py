@@ -47,11 +47,12 @@ def test_sharded_single_gpu_no_exchange(vk):
 
 
 @pytest.mark.parametrize("m", [4096, 4001])  # even split (ncclAllGather) / uneven (broadcasts)
-def test_sharded_multi_gpu_allgather(vk, m):
+@pytest.mark.parametrize("mode", [True, "pipelined"], ids=["nccl", "pipelined"])
+def test_sharded_multi_gpu_allgather(vk, m, mode):
     ngpu = torch.cuda.device_count()
     if ngpu < 2:
         pytest.skip("needs >= 2 GPUs")
-    C_parts, off, g16, g32, tc, tg = _sharded(vk, ngpu, m, 2048, 1024, allgather=True)
+    C_parts, off, g16, g32, tc, tg = _sharded(vk, ngpu, m, 2048, 1024, allgather=mode)
     for r in range(ngpu):
         c = C_parts[r].cpu().numpy()
         assert not np.isnan(c.astype(np.float32)).any(), f"GPU {r} missing rows after the all-gather"

@@ -342,11 +342,13 @@ def selftest_wait_timeout(device: int = 0, timeout_us: int = 50000) -> int:
 
 
 def gemm_sharded(A_parts, B_parts, C_parts, m: int, n: int, k: int, *, acc: str = "f32",
-                 algo: str = "auto", allgather: bool = True):
+                 algo: str = "auto", allgather=True):
     """Single-process multi-GPU row-block GEMM through ``vk_gemm_sharded``.
 
     A_parts[r]: GPU r's row slice [rows_r, k]; B_parts[r]: full [k, n] on GPU r; C_parts[r]: full
-    [m, n] buffer on GPU r.  Returns (compute_ms, gather_ms), each the max over GPUs.
+    [m, n] buffer on GPU r.  ``allgather``: False, True (NCCL after the GEMMs) or "pipelined" (peer
+    copies of finished row chunks overlapped with the GEMM).  Returns (compute_ms, gather_ms), each
+    the max over GPUs.
     """
     import torch
     g = len(A_parts)
@@ -363,7 +365,7 @@ def gemm_sharded(A_parts, B_parts, C_parts, m: int, n: int, k: int, *, acc: str 
     s.dtype = DTYPE_F16 if A_parts[0].dtype == torch.float16 else DTYPE_F32
     s.acc = _ACCS[acc]
     s.algo = _ALGOS[algo]
-    s.allgather_c = 1 if allgather else 0
+    s.allgather_c = 2 if allgather == "pipelined" else (1 if allgather else 0)
     s.times_ms = times
     check(lib.vk_gemm_sharded(ctypes.byref(s)))
     return float(times[0]), float(times[1])

@@ -59,6 +59,10 @@ struct ShardGroup {
     std::vector<ncclComm_t> comms;   // empty until the first all-gather
     std::vector<cudaStream_t> streams;
     std::vector<cudaEvent_t> ev_start, ev_compute, ev_gather;
+    // pipelined gather (allgather_c == 2): a copy stream and one "chunk done" event per chunk per GPU
+    bool peer_ready = false;
+    std::vector<cudaStream_t> copy_streams;
+    std::vector<std::vector<cudaEvent_t>> ev_chunk;
 };
 
 std::mutex g_shard_mu;
@@ -96,6 +100,39 @@ ShardGroup* find_or_create(const int32_t* devs, int n, int* rc)
     }
     g_groups.push_back(g);
     return g;
+}
+
+constexpr int kGatherChunks = 2;
+
+// Peer access between every pair of the group's GPUs and the copy streams/events of the pipelined
+// gather, once per group.
+int ensure_peer(ShardGroup* g)
+{
+    if (g->peer_ready) return VK_OK;
+    const int n = static_cast<int>(g->devices.size());
+    g->copy_streams.resize(n);
+    g->ev_chunk.assign(n, std::vector<cudaEvent_t>(kGatherChunks));
+    for (int i = 0; i < n; ++i) {
+        cudaError_t e = cudaSetDevice(g->devices[i]);
+        for (int j = 0; j < n && e == cudaSuccess; ++j) {
+            if (j == i) continue;
+            int can = 0;
+            e = cudaDeviceCanAccessPeer(&can, g->devices[i], g->devices[j]);
+            if (e == cudaSuccess && can) {
+                e = cudaDeviceEnablePeerAccess(g->devices[j], 0);
+                if (e == cudaErrorPeerAccessAlreadyEnabled) {
+                    cudaGetLastError();  // clear the sticky "already enabled" status
+                    e = cudaSuccess;
+                }
+            }
+        }
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&g->copy_streams[i], cudaStreamNonBlocking);
+        for (int q = 0; q < kGatherChunks && e == cudaSuccess; ++q)
+            e = cudaEventCreateWithFlags(&g->ev_chunk[i][q], cudaEventDisableTiming);
+        if (e != cudaSuccess) return cuda_err(e, "peer access / copy streams");
+    }
+    g->peer_ready = true;
+    return VK_OK;
 }
 
 int ensure_comms(ShardGroup* g)
@@ -139,7 +176,19 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
         cudaSetDevice(prev);
         return rc;
     }
-    const bool gather = a->allgather_c != 0 && n_gpu > 1;
+    if (a->allgather_c < 0 || a->allgather_c > 2) {
+        cudaSetDevice(prev);
+        return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: allgather_c must be 0, 1 or 2");
+    }
+    const bool pipelined = a->allgather_c == 2 && n_gpu > 1;
+    const bool gather = a->allgather_c == 1 && n_gpu > 1;
+    if (pipelined) {
+        rc = ensure_peer(g);
+        if (rc != VK_OK) {
+            cudaSetDevice(prev);
+            return rc;
+        }
+    }
     if (gather) {
         rc = ensure_comms(g);
         if (rc != VK_OK) {
@@ -160,18 +209,35 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
             rc = cuda_err(e, "shard start");
             break;
         }
-        vk_gemm_args ga = {};
-        ga.A = a->A[r];
-        ga.B = a->B[r];
-        ga.C = static_cast<char*>(a->C[r]) + static_cast<size_t>(off[r]) * a->n * esize;
-        ga.m = off[r + 1] - off[r];
-        ga.n = a->n;
-        ga.k = a->k;
-        ga.dtype = a->dtype;
-        ga.acc = a->acc;
-        ga.algo = a->algo;
-        ga.stream = g->streams[r];
-        rc = vk_gemm(&ga);
+        const int nchunks = pipelined ? kGatherChunks : 1;
+        const int64_t rows = off[r + 1] - off[r];
+        for (int q = 0; q < nchunks && rc == VK_OK; ++q) {
+            // pipelined gather: the rows of chunk q go to every peer (copy engines, NVLink) while
+            // chunk q+1 is computed
+            const int64_t c0 = rows * q / nchunks, c1 = rows * (q + 1) / nchunks;
+            vk_gemm_args ga = {};
+            ga.A = static_cast<const char*>(a->A[r]) + static_cast<size_t>(c0) * a->k * esize;
+            ga.B = a->B[r];
+            ga.C = static_cast<char*>(a->C[r]) + static_cast<size_t>(off[r] + c0) * a->n * esize;
+            ga.m = c1 - c0;
+            ga.n = a->n;
+            ga.k = a->k;
+            ga.dtype = a->dtype;
+            ga.acc = a->acc;
+            ga.algo = a->algo;
+            ga.stream = g->streams[r];
+            rc = vk_gemm(&ga);
+            if (rc != VK_OK || !pipelined) break;
+            e = cudaEventRecord(g->ev_chunk[r][q], g->streams[r]);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(g->copy_streams[r], g->ev_chunk[r][q], 0);
+            const size_t bytes = static_cast<size_t>(c1 - c0) * a->n * esize;
+            for (int peer = 0; peer < n_gpu && e == cudaSuccess; ++peer) {
+                if (peer == r || bytes == 0) continue;
+                e = cudaMemcpyPeerAsync(static_cast<char*>(a->C[peer]) + static_cast<size_t>(off[r] + c0) * a->n * esize,
+                                        a->devices[peer], ga.C, a->devices[r], bytes, g->copy_streams[r]);
+            }
+            if (e != cudaSuccess) rc = cuda_err(e, "pipelined gather");
+        }
         if (rc != VK_OK) break;
         e = cudaEventRecord(g->ev_compute[r], g->streams[r]);
         if (e != cudaSuccess) rc = cuda_err(e, "shard compute event");
@@ -202,6 +268,16 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
     float t_compute = 0.f, t_gather = 0.f;
     for (int r = 0; r < n_gpu; ++r) {
         cudaSetDevice(a->devices[r]);
+        // the gather-done event follows this GPU's peer copies as well in the pipelined mode
+        if (pipelined) cudaStreamWaitEvent(g->streams[r], g->ev_chunk[r][kGatherChunks - 1], 0);
+        if (pipelined) {
+            cudaEvent_t copies_done;
+            if (cudaEventCreateWithFlags(&copies_done, cudaEventDisableTiming) == cudaSuccess) {
+                cudaEventRecord(copies_done, g->copy_streams[r]);
+                cudaStreamWaitEvent(g->streams[r], copies_done, 0);
+                cudaEventDestroy(copies_done);
+            }
+        }
         cudaEventRecord(g->ev_gather[r], g->streams[r]);
         e = cudaStreamSynchronize(g->streams[r]);
         if (e != cudaSuccess && rc == VK_OK) rc = cuda_err(e, "shard synchronize");
@@ -216,7 +292,7 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
     cudaSetDevice(prev);
     if (rc == VK_OK && a->times_ms != nullptr) {
         a->times_ms[0] = t_compute;
-        a->times_ms[1] = gather ? t_gather : 0.f;
+        a->times_ms[1] = (gather || pipelined) ? t_gather : 0.f;
     }
     return rc;
 }
@@ -230,6 +306,10 @@ extern "C" int vk_shutdown(void)
         for (ncclComm_t c : g->comms) g_nccl.CommDestroy(c);
         for (size_t i = 0; i < g->devices.size(); ++i) {
             cudaSetDevice(g->devices[i]);
+            if (g->peer_ready) {
+                cudaStreamDestroy(g->copy_streams[i]);
+                for (cudaEvent_t ev : g->ev_chunk[i]) cudaEventDestroy(ev);
+            }
             cudaStreamDestroy(g->streams[i]);
             cudaEventDestroy(g->ev_start[i]);
             cudaEventDestroy(g->ev_compute[i]);
