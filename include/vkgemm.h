@@ -191,6 +191,10 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *                     k-slices, see "tail_nsplit"), 0 = off
  *   "tail_nsplit"     1 (default) = prefer column halves for the last wave when it is at most half
  *                     full; 0 = k-slices only
+ *   "tail_first"      1 (default) = when there is at least one full wave, k >= 2560 and the
+ *                     leftover tiles can be cut into 2..4 k-slices, those slices run before the
+ *                     whole tiles (their partial sums are reduced while the tensor pipes work on
+ *                     whole tiles); 0 = leftover tiles run last, policy of "tail_nsplit"
  *   "raster_group"    tiles along M per rasterisation group of the persistent scheduler (8)
  *   "bk_2sm256"       k per pipeline stage of the 256-column pair kernel: 128 (default, 3 stages
  *                     of 64 KB) or 64 (6 stages of 32 KB)

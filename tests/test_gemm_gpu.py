@@ -266,13 +266,22 @@ def test_repeated_launches_are_bitwise_identical(vk, shape, acc):
     assert v0.rel_frobenius(first.cpu().numpy().astype(np.float32), g32) <= max(tol, 5e-4)
 
 
-@pytest.mark.parametrize("mode", [{"tail_split": 0}, {"tail_nsplit": 0}, {"tail_nsplit": 1}],
-                         ids=["none", "ksplit", "nsplit"])
+TAIL_DEFAULTS = {"tail_split": 1, "tail_nsplit": 1, "tail_first": 1}
+
+
+@pytest.mark.parametrize("mode", [{"tail_split": 0}, {"tail_first": 1}, {"tail_first": 0, "tail_nsplit": 0},
+                                  {"tail_first": 0, "tail_nsplit": 1}],
+                         ids=["none", "ksplit-first", "ksplit-last", "nsplit"])
+# (256, 21248, 4096): one full wave + 9 tiles -> 8 slices each; (512, 21248, 4096): two full waves +
+# 18 tiles -> 4 slices each (run first); (2000, 3300, 3000): one full wave + 30 tiles -> 2 slices
+# each, ragged M, N, K; (1000, 19000, 1000): ragged M, N, K
 @pytest.mark.parametrize("shape", [(4096, 4096, 4096), (4000, 5120, 3000), (1024, 1024, 1024), (512, 768, 2048),
-                                   (4096, 4096, 1024)])
+                                   (4096, 4096, 1024), (256, 21248, 4096), (512, 21248, 4096), (2000, 3300, 3000),
+                                   (1000, 19000, 1000)])
 @pytest.mark.parametrize("acc", ["f32", "f16"])
 def test_tail_modes(vk, mode, shape, acc):
-    """Whole-tile, k-sliced and column-halved last waves all agree with the oracle."""
+    """Whole-tile, k-sliced (before or after the whole tiles) and column-halved partial waves all
+    agree with the oracle and are bitwise reproducible."""
     m, n, k = shape
     A, B = v0.make_inputs(m, n, k, 57, lo=-0.5, hi=0.5)
     try:
@@ -281,8 +290,8 @@ def test_tail_modes(vk, mode, shape, acc):
         c16, c32 = _run16(vk, A, B, acc=acc)
         again, _ = _run16(vk, A, B, acc=acc)
     finally:
-        vk.set_option("tail_split", 1)
-        vk.set_option("tail_nsplit", 1)
+        for name, val in TAIL_DEFAULTS.items():
+            vk.set_option(name, val)
     assert np.array_equal(c16.view(np.uint16), again.view(np.uint16))
     g32 = v0.v0_f16(A, B)[1]
     if acc == "f32":
@@ -292,10 +301,13 @@ def test_tail_modes(vk, mode, shape, acc):
         assert v0.rel_frobenius(c16.astype(np.float32), g32) <= FROB_F16ACC
 
 
-def test_split_gemms_on_concurrent_streams(vk):
-    """Two k-sliced GEMMs in flight on different streams must not share tail-split scratch."""
-    A1, B1 = v0.make_inputs(1024, 1024, 2048, 55)
-    A2, B2 = v0.make_inputs(1024, 1024, 2048, 56)
+@pytest.mark.parametrize("shape", [(1024, 1024, 2048), (4096, 4096, 1024)], ids=["slices-only", "slices-first"])
+def test_split_gemms_on_concurrent_streams(vk, shape):
+    """Two k-sliced GEMMs in flight on different streams must not share tail-split scratch (and,
+    with slices ahead of whole tiles, must not wait on each other's residency)."""
+    m, n, k = shape
+    A1, B1 = v0.make_inputs(m, n, k, 55)
+    A2, B2 = v0.make_inputs(m, n, k, 56)
     d = [(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()) for A, B in ((A1, B1), (A2, B2))]
     ref = [vk.gemm(a, b).clone() for a, b in d]
     torch.cuda.synchronize()

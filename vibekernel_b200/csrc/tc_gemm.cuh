@@ -26,13 +26,16 @@
 //
 // Tail split (the reference's last-wave K-split, results/ralph_loop_fable/src/matmul_f16/
 // matmul_f16_v23_wavesplit.cu:1-8 and matmul_f16_v42_shfl2.cu:182-189): with T tiles on C
-// persistent clusters, the first F*C tiles (F = T / C full waves) run whole; each of the R = T - F*C
-// tiles of the partial last wave is cut into S = C / R k-slices, so the last wave takes ~1/S of a
-// tile.  Every slice writes its fp32 partial to a workspace and bumps a per-(tile, CTA, warp)
-// arrival counter; the slice that arrives last sums all slices in slice order (its own from TMEM,
-// the others from the workspace) -- the same order whoever arrives last, so results are
-// bitwise reproducible -- writes C, and resets the counter.  Nobody waits on another CTA, so
-// the tail cannot deadlock whatever the residency.
+// persistent clusters, F*C tiles (F = T / C full waves) run whole; each of the R = T - F*C
+// remaining tiles is cut into S <= C / R k-slices, so the partial wave takes ~1/S of a tile.
+// With tail_first the slices run first (each cluster: at most one slice, then its whole tiles),
+// so their epilogues overlap the next tile's main loop.  Every slice bumps a per-(tile, CTA, warp)
+// arrival counter; all but the last arriver write their fp32 partial to a workspace and count
+// themselves as published; the last arriver waits (bounded) for those publishers -- CTAs that have
+// already arrived, so resident, and that wait on nobody: no deadlock whatever the residency --
+// sums all slices in slice order (its own from TMEM, the others from the workspace) -- the same
+// order whoever arrives last, so results are bitwise reproducible -- writes C, and resets the
+// counters.  Alternatively (nsplit) each tail tile is cut into two column halves.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -55,6 +58,10 @@ struct TcParams {
     // work units: [0, full_units) are whole tiles; then the tail tiles, each cut either into two
     // column halves (nsplit = 1: BN/2-wide MMAs, no reduction) or into `split` k-slices
     int units, full_units, split, nsplit;
+    // tail_first = 1 (k-slices only): the slice units are numbered before the whole tiles, so each
+    // cluster runs its slice first and the slice's publish / reduce epilogue overlaps the main loop
+    // of the cluster's next tile instead of ending the launch
+    int tail_first;
     float* ws;               // split partials: [tail tile][slice][CTA rank][128 rows x BN] fp32
     int* counters;           // [tail tile][CTA rank][4 epilogue warps][arrived, published]
     int clock_probe;         // 1: CTA 0 accumulates (cycles, ns, launches) into g_clock_probe
@@ -81,7 +88,22 @@ __device__ __forceinline__ Unit unit_info(const TcParams& p, int u)
 {
     Unit w;
     w.half = -1;
-    if (u < p.full_units) {
+    if (p.tail_first) {
+        // slice units [0, units - full_units) first, then whole tiles 0 .. full_units - 1
+        const int tail_units = p.units - p.full_units;
+        if (u >= tail_units) {
+            w.tile = u - tail_units;
+            w.kb0 = 0;
+            w.kb1 = p.num_kb;
+            w.slice = -1;
+        } else {
+            const int ti = u / p.split;
+            w.slice = u - ti * p.split;
+            w.tile = p.full_units + ti;
+            w.kb0 = p.num_kb * w.slice / p.split;
+            w.kb1 = p.num_kb * (w.slice + 1) / p.split;
+        }
+    } else if (u < p.full_units) {
         w.tile = u;
         w.kb0 = 0;
         w.kb1 = p.num_kb;
@@ -504,7 +526,74 @@ __global__ void __launch_bounds__(192, 1)
                     if (lane == 0) ok = wait_count_at_least(&ctr[1], p.split - 1, p.timeout_ns, kErrWaitEpilogue, 300 + q);
                     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
                     if (p.trace && warp == 2 && lane == 0 && blockIdx.x < 256) g_trace_cta[blockIdx.x][7] = globaltimer_ns();
-                    if (ok) {
+                    // The pipeline buffers double as staging only when this slice is the cluster's last
+                    // unit; otherwise the producer is already filling them for the next tile, and the
+                    // partials are read straight from L2 (one contiguous 512-byte span per warp load).
+                    const bool staged = u + num_clusters >= p.units;
+                    if (ok && !staged) {
+                        __threadfence();
+                        // The partial of the first other slice is fetched one chunk ahead, so its L2
+                        // latency overlaps the previous chunk's sums and stores.
+                        const int first = w.slice == 0 ? 1 : 0;
+                        const float4* first_src = reinterpret_cast<const float4*>(
+                            p.ws + (static_cast<size_t>(ti * p.split + first) * CG + rank) * kRegion + warp_off);
+                        float4 nxt[8];
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) nxt[jj] = __ldcg(first_src + jj * 32 + lane);
+#pragma unroll 1
+                        for (int c = 0; c < BN && col0 + c < p.N; c += 32) {
+                            uint32_t r[32];
+                            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
+                            float4 cur[8];
+#pragma unroll
+                            for (int jj = 0; jj < 8; ++jj) cur[jj] = nxt[jj];
+                            if (c + 32 < BN && col0 + c + 32 < p.N) {
+#pragma unroll
+                                for (int jj = 0; jj < 8; ++jj) nxt[jj] = __ldcg(first_src + (c + 32) * 8 + jj * 32 + lane);
+                            }
+                            tmem_ld_wait();
+                            float own[32];
+                            tmem_words_to_f32<ACC_F32>(r, own);
+                            // f = ((p_0 + p_1) + p_2) + ... in slice order, p_own taken from TMEM
+                            float f[32];
+#pragma unroll 1
+                            for (int s2 = 0; s2 < p.split; ++s2) {
+                                float4 v[8];
+                                if (s2 == w.slice) {
+#pragma unroll
+                                    for (int jj = 0; jj < 8; ++jj)
+                                        v[jj] = make_float4(own[4 * jj], own[4 * jj + 1], own[4 * jj + 2], own[4 * jj + 3]);
+                                } else if (s2 == first) {
+#pragma unroll
+                                    for (int jj = 0; jj < 8; ++jj) v[jj] = cur[jj];
+                                } else {
+                                    const float4* src = reinterpret_cast<const float4*>(
+                                        p.ws + (static_cast<size_t>(ti * p.split + s2) * CG + rank) * kRegion + warp_off +
+                                        static_cast<size_t>(c) * 32);
+#pragma unroll
+                                    for (int jj = 0; jj < 8; ++jj) v[jj] = __ldcg(src + jj * 32 + lane);
+                                }
+                                if (s2 == 0) {
+#pragma unroll
+                                    for (int jj = 0; jj < 8; ++jj) {
+                                        f[4 * jj] = v[jj].x;
+                                        f[4 * jj + 1] = v[jj].y;
+                                        f[4 * jj + 2] = v[jj].z;
+                                        f[4 * jj + 3] = v[jj].w;
+                                    }
+                                } else {
+#pragma unroll
+                                    for (int jj = 0; jj < 8; ++jj) {
+                                        f[4 * jj] += v[jj].x;
+                                        f[4 * jj + 1] += v[jj].y;
+                                        f[4 * jj + 2] += v[jj].z;
+                                        f[4 * jj + 3] += v[jj].w;
+                                    }
+                                }
+                            }
+                            store_rows(p, stg, row0, lane, col0 + c, f);
+                        }
+                    } else if (ok) {
                         __threadfence();
                         if (lane == 0) fence_proxy_async_global();  // published partials precede the bulk reads
                         // Columns per round so that the other (split - 1) slices' partials of this warp's

@@ -113,6 +113,7 @@ static DeviceState g_dev[kMaxDevices];
 static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 static std::atomic<int> g_tail_split{1};
 static std::atomic<int> g_tail_nsplit{1};
+static std::atomic<int> g_tail_first{1};
 static std::atomic<int> g_raster_group{8};
 // k depth per pipeline stage of the 256-column pair kernel.  Every stage ends with tcgen05.commit
 // to both CTAs' "empty" barriers, and those commits measurably throttle the tensor pipe; 128-deep
@@ -287,23 +288,33 @@ static int ensure_pack(DeviceState& st, int dev, cudaStream_t stream, int which,
 // Work decomposition of the persistent tensor-core kernels: whole tiles for the full waves,
 // and the tiles of a partial last wave cut into k-slices (at least kMinSliceKb k-blocks each).
 struct Schedule {
-    int units, full_units, split, nsplit, grid_units;
+    int units, full_units, split, nsplit, tail_first, grid_units;
 };
 
 static constexpr int kMinSliceKb = 4;
 static constexpr int kMaxSplit = 8;
 
-// Tail policy.  With R tail tiles on C clusters: when 2R <= C and the layout allows it, each tail tile
-// is cut into two column halves (MMA N = BN/2, no partial sums), which measured clearly faster than
-// k-slices for the last wave (the k-slice path pays for publishing and reducing fp32 partials); when
-// R <= C/4 the tiles are cut into up to 8 k-slices instead, which parallelises small problems more.
-static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool allow_split, bool allow_nsplit)
+// Tail policy.  With R tail tiles on C clusters, at least one full wave, S = C / R k-slices in
+// 2..4 and K >= kFirstMinK, the tail tiles are cut into S k-slices that run FIRST (tail_first): the
+// fp32 partials are published and reduced while the clusters' whole tiles keep the tensor pipes
+// busy, and the MMAs keep the full-width tile shape (measured on B200: +2 to +5 % over column
+// halves at 4096^3, 5120^3, 4000x5120x3000, 2048x8192x4096, even at 4096^2 x 3072; slower for
+// K <= 2048 or S = 8, where the reduction outlasts the next tile's main loop).  Otherwise, when 2R <= C and the layout allows
+// it, each tail tile is cut into two column halves (MMA N = BN/2, no partial sums; they move 1.5x
+// the operand bytes per MMA cycle of a whole tile).  When R <= C/4 the tiles are cut into up to 8
+// k-slices instead, which parallelises small problems more.
+static constexpr long long kFirstMinK = 2560;
+static constexpr int kFirstMaxSplit = 4;
+
+static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool allow_split, bool allow_nsplit,
+                              bool allow_first)
 {
     Schedule sc;
     sc.units = static_cast<int>(tiles);
     sc.full_units = static_cast<int>(tiles);
     sc.split = 1;
     sc.nsplit = 0;
+    sc.tail_first = 0;
     if (allow_split && tiles > 0) {
         const long long full_waves = tiles / max_units;
         const long long rem = tiles - full_waves * max_units;
@@ -312,7 +323,12 @@ static Schedule plan_schedule(long long tiles, int num_kb, int max_units, bool a
             if (s > num_kb / kMinSliceKb) s = num_kb / kMinSliceKb;
             if (s > kMaxSplit) s = kMaxSplit;
             const bool ksplit_better = 4 * rem <= max_units && s >= 4;
-            if (allow_nsplit && 2 * rem <= max_units && !ksplit_better) {
+            if (allow_first && full_waves >= 1 && s >= 2 && s <= kFirstMaxSplit) {
+                sc.full_units = static_cast<int>(full_waves * max_units);
+                sc.split = static_cast<int>(s);
+                sc.tail_first = 1;
+                sc.units = static_cast<int>(sc.full_units + rem * s);
+            } else if (allow_nsplit && 2 * rem <= max_units && !ksplit_better) {
                 sc.full_units = static_cast<int>(full_waves * max_units);
                 sc.nsplit = 1;
                 sc.units = static_cast<int>(sc.full_units + 2 * rem);
@@ -418,11 +434,13 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     // n-split halves need whole 64-column boxes per CTA and N-major B tiles
     const bool nsplit_ok = (Cfg::kBNCta / 2) % 64 == 0 && !pb.trans_b && g_tail_nsplit.load(std::memory_order_relaxed);
     const Schedule sc =
-        plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0, nsplit_ok);
+        plan_schedule(tiles, p.num_kb, max_units, g_tail_split.load(std::memory_order_relaxed) != 0, nsplit_ok,
+                      g_tail_first.load(std::memory_order_relaxed) != 0 && pb.k >= kFirstMinK);
     p.units = sc.units;
     p.full_units = sc.full_units;
     p.split = sc.split;
     p.nsplit = sc.nsplit;
+    p.tail_first = sc.tail_first;
     p.ws = nullptr;
     p.counters = nullptr;
     if (sc.split > 1 && fixed != nullptr) {
@@ -902,6 +920,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
     }
     if (strcmp(name, "tail_nsplit") == 0) {
         g_tail_nsplit.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
+    if (strcmp(name, "tail_first") == 0) {
+        g_tail_first.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
     if (strcmp(name, "raster_group") == 0) {
