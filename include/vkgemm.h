@@ -195,6 +195,9 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *                     leftover tiles can be cut into 2..4 k-slices, those slices run before the
  *                     whole tiles (their partial sums are reduced while the tensor pipes work on
  *                     whole tiles); 0 = leftover tiles run last, policy of "tail_nsplit"
+ *   "tma_store"       1 (default) = the tensor-core kernels write fp16 C with TMA tile stores when C
+ *                     is 16-byte aligned with a pitch that is a multiple of 8 elements; 0 = always
+ *                     per-lane coalesced stores (the path taken for any other C)
  *   "raster_group"    tiles along M per rasterisation group of the persistent scheduler (8)
  *   "bk_2sm256"       k per pipeline stage of the 256-column pair kernel: 128 (default, 3 stages
  *                     of 64 KB) or 64 (6 stages of 32 KB)

@@ -215,9 +215,11 @@ def test_sgemm_v1_and_v2_agree(vk, shape):
         assert v0.rel_frobenius(c.cpu().numpy(), g) <= FROB_SGEMM
 
 
+@pytest.mark.parametrize("tma_store", [1, 0], ids=["tma-store", "lane-stores"])
 @pytest.mark.parametrize("dtype", ["f16", "f32"])
-def test_canary_and_strides(vk, dtype):
-    """C written through ldc > n inside a sentinel-filled buffer: nothing outside C changes."""
+def test_canary_and_strides(vk, dtype, tma_store):
+    """C written through ldc > n inside a sentinel-filled buffer: nothing outside C changes (the
+    fp16 C here is TMA-store eligible: 16-byte aligned, pitch a multiple of 8, ragged last box)."""
     m, n, k, pad = 300, 264, 136, 40
     if dtype == "f16":
         A, B = v0.make_inputs(m, n, k, 41)
@@ -230,8 +232,12 @@ def test_canary_and_strides(vk, dtype):
     # A and B with row pitch > row length as well
     Abig = torch.zeros((m, k + 24), dtype=tdt, device="cuda")
     Abig[:, :k] = torch.from_numpy(A).cuda()
-    vk.gemm(Abig[:, :k], torch.from_numpy(B).cuda(), C)
-    torch.cuda.synchronize()
+    vk.set_option("tma_store", tma_store)
+    try:
+        vk.gemm(Abig[:, :k], torch.from_numpy(B).cuda(), C)
+        torch.cuda.synchronize()
+    finally:
+        vk.set_option("tma_store", 1)
     out = big.cpu().numpy().astype(np.float32)
     mask = np.ones_like(out, dtype=bool)
     mask[1:m + 1, 8:8 + n] = False
@@ -345,11 +351,11 @@ def test_tail_split_matches_unsplit(vk, shape):
         assert v0.max_elem_rel(c, g32) <= ELEM
 
 
-PIPELINE_OPTIONS = [{"bk_2sm256": 64}, {"bk_2sm256": 64, "tail_split": 0}, {"tail_split": 0}]
-_DEFAULTS = {"bk_2sm256": 128, "tail_split": 1}
+PIPELINE_OPTIONS = [{"bk_2sm256": 64}, {"bk_2sm256": 64, "tail_split": 0}, {"tail_split": 0}, {"tma_store": 0}]
+_DEFAULTS = {"bk_2sm256": 128, "tail_split": 1, "tma_store": 1}
 
 
-@pytest.mark.parametrize("opts", PIPELINE_OPTIONS, ids=["bk64", "bk64-nosplit", "bk128-nosplit"])
+@pytest.mark.parametrize("opts", PIPELINE_OPTIONS, ids=["bk64", "bk64-nosplit", "bk128-nosplit", "lane-stores"])
 @pytest.mark.parametrize("shape", [(1024, 1024, 1024), (4096, 4096, 4096), (4000, 5120, 3000), (200, 136, 72),
                                    (256, 256, 4096)])
 @pytest.mark.parametrize("acc", ["f32", "f16"])

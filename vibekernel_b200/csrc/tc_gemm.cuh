@@ -54,6 +54,7 @@ struct TcParams {
     long long ldc;
     float* C32;              // optional fp32 copy, ld = N
     int vec_ok;              // C / C32 alignment allows 16-byte stores
+    int c_tma;               // 1: fp16 C is written by TMA tile stores through the C tensor map
     unsigned long long timeout_ns;
     // work units: [0, full_units) are whole tiles; then the tail tiles, each cut either into two
     // column halves (nsplit = 1: BN/2-wide MMAs, no reduction) or into `split` k-slices
@@ -126,9 +127,13 @@ __device__ __forceinline__ Unit unit_info(const TcParams& p, int u)
     return w;
 }
 
-// Bytes of the per-warp staging buffer of the epilogue: 32 rows x 32 fp16 = 64 B, pitch 80 B.
+// Epilogue staging per warp: two 2 KB buffers of 32 rows x 32 fp16 in the 64-byte swizzle layout of
+// the C tensor map (TMA stores, double-buffered), or, when C cannot take TMA stores, one buffer of
+// 32 rows at an 80-byte pitch (bank-conflict-free row writes, 64-byte runs read back).
 constexpr int kEpiPitch = 80;
-constexpr int kEpiWarpBytes = 32 * kEpiPitch;
+constexpr int kEpiBufBytes = 32 * 64;
+constexpr int kEpiWarpBytes = 2 * kEpiBufBytes;
+static_assert(kEpiWarpBytes >= 32 * kEpiPitch, "fallback staging fits the warp's area");
 
 template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
 struct TcCfg {
@@ -150,7 +155,8 @@ struct TcCfg {
     // 48 KB per epilogue warp.
     static constexpr int kRedFloatsPerWarp = 12288;
     static constexpr int kSmemBytes =
-        1024 /*alignment slack*/ + STAGES * kStageBytes + kNumBars * 8 + 32 + 4 * kEpiWarpBytes;
+        1024 /*alignment slack*/ + STAGES * kStageBytes + kNumBars * 8 + 32 + 1024 /*staging alignment*/ +
+        4 * kEpiWarpBytes;
     static constexpr int kThreads = 192;
     static_assert(CG == 1 || CG == 2, "cta group");
     static_assert(KA == 1 || KA == 2, "k spans per stage");
@@ -193,10 +199,13 @@ __device__ __forceinline__ void tmem_words_to_f32(const uint32_t (&r)[32], float
 
 // One warp writes its 32 rows x 32 columns of C (this lane's row = row0 + lane, values f for
 // columns col .. col+31): the fused epilogue and the fp32 copy are applied per row, then the fp16
-// results go through the warp's staging buffer so that each global store instruction writes 64-byte
-// runs of 8 rows (4 lanes per row) instead of 16 bytes of 32 different rows.
-__device__ __forceinline__ void store_rows(const TcParams& p, uint8_t* stg, int row0, int lane, int col,
-                                           float (&f)[32])
+// results go through the warp's staging buffer.  With a C tensor map (c_tma) lane 0 stores the
+// 32 x 32 box with one TMA store (the box is clipped to M x N by the hardware); the two buffers
+// alternate, and a buffer is rewritten only after the store issued from it two chunks earlier has
+// read it.  Otherwise each global store instruction writes 64-byte runs of 8 rows (4 lanes per row)
+// instead of 16 bytes of 32 different rows.
+__device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap* tmap_c, uint8_t* stg, int row0,
+                                           int lane, int col, float (&f)[32], uint32_t& nbuf)
 {
     const int row = row0 + lane;
     if (p.ep && row < p.M) {
@@ -223,6 +232,26 @@ __device__ __forceinline__ void store_rows(const TcParams& p, uint8_t* stg, int 
             for (int i = 0; i < 32; ++i)
                 if (col + i < p.N) d32[i] = f[i];
         }
+    }
+    if (p.c_tma) {
+        uint8_t* buf = stg + (nbuf & 1u) * kEpiBufBytes;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        // 64-byte swizzle: 16-byte chunk j of row r sits at chunk j ^ ((r >> 1) & 3)
+        uint4* srow = reinterpret_cast<uint4*>(buf + lane * 64);
+        const int sw = (lane >> 1) & 3;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            srow[j ^ sw] = make_uint4(pack_half2(f[8 * j], f[8 * j + 1]), pack_half2(f[8 * j + 2], f[8 * j + 3]),
+                                      pack_half2(f[8 * j + 4], f[8 * j + 5]), pack_half2(f[8 * j + 6], f[8 * j + 7]));
+        fence_proxy_async_smem();  // the generic-proxy writes precede the TMA engine's reads
+        __syncwarp();
+        if (lane == 0 && row0 < p.M) {
+            tma_store_2d(tmap_c, smem_u32(buf), col, row0);
+            bulk_commit_group();
+        }
+        ++nbuf;
+        return;
     }
     uint4* srow = reinterpret_cast<uint4*>(stg + lane * kEpiPitch);
 #pragma unroll
@@ -255,7 +284,7 @@ __device__ __forceinline__ void store_rows(const TcParams& p, uint8_t* stg, int 
 template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
 __global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const TcParams p)
+                   const __grid_constant__ CUtensorMap tmap_c, const TcParams p)
 {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
     using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32>;
@@ -266,7 +295,9 @@ __global__ void __launch_bounds__(192, 1)
     uint8_t* sB = smem + STAGES * Cfg::kABytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::kBBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
-    uint8_t* epi_stage = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_slot) + 4 + 15) & ~uintptr_t(15));
+    // 1024-byte aligned: the 64-byte swizzle pattern of the TMA stores is a function of address bits
+    uint8_t* epi_stage =
+        reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tmem_slot) + 4 + 1023) & ~uintptr_t(1023));
 
     const uint32_t bar0 = smem_u32(bars);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -296,6 +327,7 @@ __global__ void __launch_bounds__(192, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
+        if (p.c_tma) prefetch_tmap(&tmap_c);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
@@ -476,6 +508,7 @@ __global__ void __launch_bounds__(192, 1)
         // ------------------------------------------------------------------ epilogue
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         int it = 0;
+        uint32_t nbuf = 0;       // 32-column chunks stored so far (staging buffer parity)
         for (int u = cluster_id; u < p.units; u += num_clusters, ++it) {
             const Unit w = unit_info(p, u);
             const int acc = it & 1;
@@ -591,7 +624,7 @@ __global__ void __launch_bounds__(192, 1)
                                     }
                                 }
                             }
-                            store_rows(p, stg, row0, lane, col0 + c, f);
+                            store_rows(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                         }
                     } else if (ok) {
                         __threadfence();
@@ -660,7 +693,7 @@ __global__ void __launch_bounds__(192, 1)
                                         }
                                     }
                                 }
-                                store_rows(p, stg, row0, lane, col0 + c, f);
+                                store_rows(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                             }
                             __syncwarp();
                         }
@@ -679,7 +712,7 @@ __global__ void __launch_bounds__(192, 1)
                     if (col0 + c < p.N) {
                         float f[32];
                         tmem_words_to_f32<ACC_F32>(r, f);
-                        store_rows(p, stg, row0, lane, col0 + c, f);
+                        store_rows(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                     }
                 }
             }
@@ -696,6 +729,7 @@ __global__ void __launch_bounds__(192, 1)
                     mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
             }
         }
+        if (p.c_tma && lane == 0) bulk_wait_group_all();  // C written before the CTA exits
     }
 
     tc_fence_before();

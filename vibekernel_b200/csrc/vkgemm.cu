@@ -81,8 +81,26 @@ struct FixedScratch {
     size_t ws_bytes, ctr_bytes;
 };
 
+// One encoded tensor map, keyed by everything the encoding depends on.  A map holds only the base
+// address, shape, pitch and box, so a hit stays valid even after the buffer is freed and another
+// allocation reuses the address.
+struct TmapEntry {
+    const void* base = nullptr;
+    int64_t rows = 0, cols = 0, ld = 0;
+    uint32_t box_cols = 0, box_rows = 0;
+    int kind = -1;  // 0 = operand (128-byte swizzle), 1 = C store map (64-byte swizzle)
+    CUtensorMap map;
+};
+
 struct DeviceState {
     std::atomic<bool> ready{false};
+    // Recently encoded tensor maps (round-robin replacement): the reference driver's loop calls
+    // with the same pointers and shapes every iteration, and encoding costs host time that sits
+    // between its start event and the kernel.
+    static constexpr int kTmapCache = 16;
+    std::mutex tmap_mu;
+    TmapEntry tmaps[kTmapCache];
+    int tmap_next = 0;
     // Device address of this file's static no-allocation scratch array, looked up once per device
     // by the first vk_gemm_noalloc call made with the device current.
     std::atomic<void*> noalloc_scratch{nullptr};
@@ -114,6 +132,7 @@ static std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 static std::atomic<int> g_tail_split{1};
 static std::atomic<int> g_tail_nsplit{1};
 static std::atomic<int> g_tail_first{1};
+static std::atomic<int> g_tma_store{1};
 static std::atomic<int> g_raster_group{8};
 // k depth per pipeline stage of the 256-column pair kernel.  Every stage ends with tcgen05.commit
 // to both CTAs' "empty" barriers, and those commits measurably throttle the tensor pipe; 128-deep
@@ -364,6 +383,51 @@ static int make_tmap_f16(CUtensorMap* map, const void* base, int64_t rows, int64
     return VK_OK;
 }
 
+// 2-D fp16 tensor map for the TMA stores of C: 32 x 32 boxes in the 64-byte swizzle layout of the
+// kernel's epilogue staging buffers.
+static int make_tmap_c(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld)
+{
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(VK_ERR_CUDA, "cuTensorMapEncodeTiled (C) failed (%d) rows=%lld cols=%lld ld=%lld", (int)r,
+                         (long long)rows, (long long)cols, (long long)ld);
+    return VK_OK;
+}
+
+// make_tmap_f16 (kind 0) / make_tmap_c (kind 1) through the device's cache.
+static int cached_tmap(DeviceState& st, int kind, CUtensorMap* out, const void* base, int64_t rows, int64_t cols,
+                       int64_t ld, uint32_t box_cols, uint32_t box_rows)
+{
+    std::lock_guard<std::mutex> lk(st.tmap_mu);
+    for (const TmapEntry& e : st.tmaps) {
+        if (e.kind == kind && e.base == base && e.rows == rows && e.cols == cols && e.ld == ld &&
+            e.box_cols == box_cols && e.box_rows == box_rows) {
+            *out = e.map;
+            return VK_OK;
+        }
+    }
+    const int rc = kind == 0 ? make_tmap_f16(out, base, rows, cols, ld, box_cols, box_rows)
+                             : make_tmap_c(out, base, rows, cols, ld);
+    if (rc != VK_OK) return rc;
+    TmapEntry& e = st.tmaps[st.tmap_next];
+    st.tmap_next = (st.tmap_next + 1) % DeviceState::kTmapCache;
+    e.base = base;
+    e.rows = rows;
+    e.cols = cols;
+    e.ld = ld;
+    e.box_cols = box_cols;
+    e.box_rows = box_rows;
+    e.kind = kind;
+    e.map = *out;
+    return VK_OK;
+}
+
 // ------------------------------------------------------------------------------------------
 // Launchers
 // ------------------------------------------------------------------------------------------
@@ -396,11 +460,11 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     CUtensorMap ta, tb;
     // A: K-major boxes of 64 k x 128 rows, or (A stored k x m) M-major boxes of 64 rows x BK k.
     // B: N-major boxes of 64 columns x BK k, or (B stored n x k) K-major boxes of 64 k x BN/CG rows.
-    rc = pb.trans_a ? make_tmap_f16(&ta, pb.A, pb.k, pb.m, pb.lda, 64, Cfg::kBK)
-                    : make_tmap_f16(&ta, pb.A, pb.m, pb.k, pb.lda, 64, Cfg::kBM);
+    rc = pb.trans_a ? cached_tmap(st, 0, &ta, pb.A, pb.k, pb.m, pb.lda, 64, Cfg::kBK)
+                    : cached_tmap(st, 0, &ta, pb.A, pb.m, pb.k, pb.lda, 64, Cfg::kBM);
     if (rc != VK_OK) return rc;
-    rc = pb.trans_b ? make_tmap_f16(&tb, pb.B, pb.n, pb.k, pb.ldb, 64, Cfg::kBNCta)
-                    : make_tmap_f16(&tb, pb.B, pb.k, pb.n, pb.ldb, 64, Cfg::kBK);
+    rc = pb.trans_b ? cached_tmap(st, 0, &tb, pb.B, pb.n, pb.k, pb.ldb, 64, Cfg::kBNCta)
+                    : cached_tmap(st, 0, &tb, pb.B, pb.k, pb.n, pb.ldb, 64, Cfg::kBK);
     if (rc != VK_OK) return rc;
 
     TcParams p;
@@ -417,6 +481,15 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     const bool c_vec = (reinterpret_cast<uintptr_t>(pb.C) % 16 == 0) && (pb.ldc % 8 == 0);
     const bool c32_vec = pb.C32 == nullptr || ((reinterpret_cast<uintptr_t>(pb.C32) % 16 == 0) && (pb.n % 4 == 0));
     p.vec_ok = (c_vec && c32_vec) ? 1 : 0;
+    // TMA stores of C need a 16-byte aligned base and a pitch that is a multiple of 16 bytes
+    CUtensorMap tc;
+    memset(&tc, 0, sizeof(tc));
+    p.c_tma = (g_tma_store.load(std::memory_order_relaxed) && c_vec && pb.m > 0 && pb.n > 0 &&
+               pb.ldc * 2 < (1LL << 40)) ? 1 : 0;
+    if (p.c_tma) {
+        rc = cached_tmap(st, 1, &tc, pb.C, pb.m, pb.n, pb.ldc, 32, 32);
+        if (rc != VK_OK) return rc;
+    }
     p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
     p.clock_probe = g_clock_probe_on.load(std::memory_order_relaxed);
     p.a_mn = pb.trans_a;
@@ -475,7 +548,7 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     cfg.stream = pb.stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    VK_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, ta, tb, p));
+    VK_CUDA_TRY(cudaLaunchKernelEx(&cfg, fn, ta, tb, tc, p));
     return VK_OK;
 }
 
@@ -592,7 +665,8 @@ static bool tma_ok_f16(const void* p, int64_t ld)
 
 int dispatch(DeviceState& st, int dev, const Problem& pb, int dtype, int acc, int algo);
 
-// Frees every device's tail-split workspace (called from vk_shutdown).
+// Frees every device's tail-split workspace and forgets its cached tensor maps (called from
+// vk_shutdown).
 void release_device_state()
 {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -600,6 +674,11 @@ void release_device_state()
     cudaGetDevice(&prev);
     for (int d = 0; d < kMaxDevices; ++d) {
         DeviceState& st = g_dev[d];
+        {
+            std::lock_guard<std::mutex> tl(st.tmap_mu);
+            for (TmapEntry& e : st.tmaps) e = TmapEntry();
+            st.tmap_next = 0;
+        }
         if (st.num_scratch == 0) continue;
         cudaSetDevice(d);
         for (int i = 0; i < st.num_scratch; ++i) {
@@ -924,6 +1003,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
     }
     if (strcmp(name, "tail_first") == 0) {
         g_tail_first.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
+    if (strcmp(name, "tma_store") == 0) {
+        g_tma_store.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
     if (strcmp(name, "raster_group") == 0) {
