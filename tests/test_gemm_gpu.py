@@ -198,6 +198,24 @@ def test_sgemm_ragged(vk, shape):
     assert v0.rel_frobenius(c, g) <= FROB_SGEMM
 
 
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1000, 1000, 1000), (300, 200, 20), (129, 260, 36)])
+def test_sgemm_paired_fma_bitwise(vk, shape):
+    """The paired-FMA SGEMM performs every element's fused multiply-adds in the same order as the
+    scalar-FMA kernel: the two results are bitwise equal."""
+    m, n, k = shape
+    A, B = v0.make_inputs(m, n, k, 33, dist="normal", dtype=np.float32)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    paired = vk.gemm(dA, dB)
+    try:
+        vk.set_option("sgemm_paired", 0)
+        scalar = vk.gemm(dA, dB)
+    finally:
+        vk.set_option("sgemm_paired", 1)
+    torch.cuda.synchronize()
+    assert torch.equal(paired.view(torch.int32), scalar.view(torch.int32))
+    assert v0.rel_frobenius(paired.cpu().numpy(), v0.v0_f32(A, B)) <= FROB_SGEMM
+
+
 @pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1000, 1000, 1000), (300, 200, 20)])
 def test_sgemm_v1_and_v2_agree(vk, shape):
     m, n, k = shape

@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_kernel(const SgemmPa
 
 // ---------------------------------------------------------------------------------------------
 // sgemm_ffma_v2_kernel -- the default fp32 SGEMM for 16-byte-aligned A/B with lda, ldb multiples
-// of 4.  128 x 128 CTA tile, BK = 16, 256 threads, 8 x 8 outputs per thread in four 4 x 4
+// of 4 (inner product on the paired FMA by default, see PAIRED below).  128 x 128 CTA tile, BK = 16, 256 threads, 8 x 8 outputs per thread in four 4 x 4
 // quadrants.  Operands move global -> shared with cp.async (16-byte, zero-filled at the edges) in a
 // 3-stage ring, so no registers stage the next tile and three k-tiles are in flight.  A stays
 // K-contiguous in shared memory (rows padded to 20 floats so the two rows a warp reads per
@@ -223,6 +223,12 @@ __device__ __forceinline__ void sg2_load_stage(const SgemmParams& p, float* As, 
     }
 }
 
+// PAIRED: the inner product runs on the paired fp32 FMA of sm_100 (__ffma2_rn: two independent
+// round-to-nearest fused multiply-adds per instruction, so every output element sees exactly the same
+// operations in the same order as with fmaf): each row's A value is broadcast into a pair and
+// multiplied into 4 pairs of adjacent B columns.  It halves the FMA instructions per output, and
+// the scalar kernel is limited by instruction dispatch, not by the FMA pipe or by memory.
+template <bool PAIRED>
 __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_v2_kernel(const SgemmParams p)
 {
     extern __shared__ __align__(16) float sg2_smem[];
@@ -238,6 +244,11 @@ __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_v2_kernel(const Sgem
     for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    float2 acc2[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc2[i][j] = make_float2(0.f, 0.f);
 
 #pragma unroll
     for (int s = 0; s < kSg2Stages - 1; ++s) {
@@ -264,17 +275,38 @@ __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_v2_kernel(const Sgem
             for (int kk = 0; kk < 4; ++kk) {
                 const float4 b0 = *reinterpret_cast<const float4*>(b_s + (kc + kk) * kSgBN + tx * 4);
                 const float4 b1 = *reinterpret_cast<const float4*>(b_s + (kc + kk) * kSgBN + tx * 4 + 64);
-                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                if constexpr (PAIRED) {
+                    const float2 bp[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                                          make_float2(b1.z, b1.w)};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float av = kk == 0 ? a4[i].x : kk == 1 ? a4[i].y : kk == 2 ? a4[i].z : a4[i].w;
+                    for (int i = 0; i < 8; ++i) {
+                        const float av = kk == 0 ? a4[i].x : kk == 1 ? a4[i].y : kk == 2 ? a4[i].z : a4[i].w;
+                        const float2 ap = make_float2(av, av);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av, bv[j], acc[i][j]);
+                        for (int j = 0; j < 4; ++j) acc2[i][j] = __ffma2_rn(ap, bp[j], acc2[i][j]);
+                    }
+                } else {
+                    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float av = kk == 0 ? a4[i].x : kk == 1 ? a4[i].y : kk == 2 ? a4[i].z : a4[i].w;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av, bv[j], acc[i][j]);
+                    }
                 }
             }
         }
     }
     cp_async_wait<0>();
+    if constexpr (PAIRED) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[i][2 * j] = acc2[i][j].x;
+                acc[i][2 * j + 1] = acc2[i][j].y;
+            }
+    }
 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {

@@ -139,6 +139,7 @@ static std::atomic<int> g_raster_group{8};
 // stages (3 x 64 KB) halve them per MMA and beat 64-deep ones (6 x 32 KB) at every size measured.
 static std::atomic<int> g_bk_2sm256{128};
 static std::atomic<int> g_sgemm_v2{1};
+static std::atomic<int> g_sgemm_paired{1};
 static std::atomic<int> g_repack{1};
 static std::atomic<int> g_clock_probe_on{0};
 static std::atomic<int> g_trace_on{0};
@@ -593,16 +594,18 @@ static int launch_sgemm(const Problem& pb)
     dim3 grid(static_cast<unsigned>((pb.n + kSgBN - 1) / kSgBN), static_cast<unsigned>((pb.m + kSgBM - 1) / kSgBM));
     if (grid.y > 65535u) return set_error(VK_ERR_UNSUPPORTED, "m too large for the SGEMM grid");
     if (p.vec_a && p.vec_b && g_sgemm_v2.load(std::memory_order_relaxed)) {
-        static std::atomic<int> attr_dev_mask{0};  // smem attribute set once per device (bit per ordinal < 31)
+        // smem attribute set once per device (bit per ordinal < 31) and kernel
+        static std::atomic<int> attr_dev_mask[2] = {{0}, {0}};
+        const int paired = g_sgemm_paired.load(std::memory_order_relaxed) != 0 ? 1 : 0;
+        auto fn = paired ? sgemm_ffma_v2_kernel<true> : sgemm_ffma_v2_kernel<false>;
         int dev = 0;
         VK_CUDA_TRY(cudaGetDevice(&dev));
         const int bit = 1 << (dev & 31);
-        if (!(attr_dev_mask.load() & bit)) {
-            VK_CUDA_TRY(cudaFuncSetAttribute(sgemm_ffma_v2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSg2SmemBytes));
-            attr_dev_mask.fetch_or(bit);
+        if (!(attr_dev_mask[paired].load() & bit)) {
+            VK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSg2SmemBytes));
+            attr_dev_mask[paired].fetch_or(bit);
         }
-        sgemm_ffma_v2_kernel<<<grid, kSgThreads, kSg2SmemBytes, pb.stream>>>(p);
+        fn<<<grid, kSgThreads, kSg2SmemBytes, pb.stream>>>(p);
     } else {
         sgemm_ffma_kernel<<<grid, kSgThreads, 0, pb.stream>>>(p);
     }
@@ -1025,6 +1028,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
     }
     if (strcmp(name, "sgemm_v2") == 0) {
         g_sgemm_v2.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
+    if (strcmp(name, "sgemm_paired") == 0) {
+        g_sgemm_paired.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
     if (strcmp(name, "trace") == 0) {
