@@ -12,7 +12,9 @@ fit in the 126 MB L2.
 
 Multi-GPU (torchrun, one process per GPU): every rank computes its own 4096-row block of a
 (4096*N) x 4096 x 4096 GEMM with B replicated (row-block sharding, weak scaling, no exchange on
-the data path); `--allgather` adds the NCCL all-gather of C.  `--workload shard16k` is the
+the data path); `--allgather` adds the NCCL all-gather of C after the GEMM, `--allgather pipelined`
+the copy-engine gather overlapped with it (row chunks pushed into the peers' C as they finish).
+`--workload shard16k` is the
 16384^3 strong-scaling case (M split across ranks).
 """
 from __future__ import annotations
@@ -194,7 +196,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rubric")
     ap.add_argument("--algo", default="auto")
     ap.add_argument("--tile-n", type=int, default=0)
-    ap.add_argument("--allgather", action="store_true")
+    ap.add_argument("--allgather", nargs="?", const="nccl", default=None, choices=["nccl", "pipelined"],
+                    help="all-gather C on every rank: nccl = NCCL after the GEMM (default when given); "
+                         "pipelined = copy-engine peer pushes of finished row chunks overlapped with the GEMM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -245,11 +249,23 @@ def main():
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    def local_gemm(a, b, out):
+        vk.gemm(a, b, out, acc=acc, algo=args.algo, tile_n=args.tile_n, stream=stream)
+
+    peer_gather = None
+    launches_per_step = 1
+    if C_full is not None and args.allgather == "pipelined":
+        peer_gather = dist_gemm.PeerRowGather(C_full, off, rank)
+        launches_per_step = len(dist_gemm.chunk_rows(rows, 2))
+
     def step():
-        vk.gemm(A, B, C, acc=acc, algo=args.algo, tile_n=args.tile_n, stream=stream)
+        if peer_gather is not None:
+            peer_gather.run(A, B, local_gemm, chunks=2)  # GEMM chunks + overlapped peer pushes
+        else:
+            local_gemm(A, B, C)
 
     def gather():
-        if C_full is not None:
+        if C_full is not None and peer_gather is None:
             dist_gemm.allgather_rows(C_full, off, rank)
 
     def barrier():
@@ -350,7 +366,7 @@ def main():
             "dtype": dt, "data": "synthetic (seeded uniform/normal inputs, BASELINE shapes)",
             "config": {"workload": label, "m": m_total, "n": n, "k": k, "m_per_gpu": rows, "acc": acc,
                        "algo": args.algo, "tile_n": args.tile_n or 256, "parallelism": f"rowshard{world}",
-                       "allgather_c": bool(C_full is not None),
+                       "allgather_c": (args.allgather if C_full is not None else False),
                        "l2": "flushed before every timed call (256 MiB write outside the event pair)",
                        "timing": "per-call CUDA events + event synchronize (reference main.cpp loop)"},
             "roofline": roof,
@@ -358,7 +374,7 @@ def main():
             "clocks": dict(clocks.summary(), kernel_sm_mhz=(round(kernel_mhz, 1) if kernel_mhz else None)),
             "clock_true_peak_frac": (round(achieved / (148 * 8192 * kernel_mhz * 1e6 / 1e12), 4)
                                      if (kernel_mhz and dt == "f16") else None),
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * launches_per_step,
             "e2e": e2e,
         }
         if C_full is not None:
@@ -374,6 +390,8 @@ def main():
                 "kind": "reference" if v0.ref_available() else "port",
                 "sample": f"reference v0 (oracle/_ref) on {rws} of {m_cfg} rows ({secs:.2f} s), OpenBLAS {threads} threads"}
         print(json.dumps(line), flush=True)
+    if peer_gather is not None:
+        peer_gather.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -167,6 +167,26 @@ typedef struct vk_shard_args {
 
 int vk_gemm_sharded(const vk_shard_args* args);
 
+/* Peer-memory plumbing for one-process-per-GPU jobs (torchrun), no counterpart in the reference:
+ * the pipelined all-gather of the row-sharded GEMM (vibekernel_b200/dist_gemm.py) maps every
+ * peer's full C buffer into its own process and pushes each finished chunk of its rows into them
+ * with the copy engines over NVLink while the next chunk is computed.
+ *   vk_ipc_export   CUDA IPC handle of the allocation holding device buffer `ptr`, plus the
+ *                   buffer's byte offset inside it (allocators hand out pieces of allocations);
+ *   vk_ipc_import   map a handle exported by ANOTHER process on this node into this process
+ *                   (plain peer mapping, lazy peer access); *out_ptr = the peer's buffer;
+ *   vk_ipc_release  unmap a pointer returned by vk_ipc_import;
+ *   vk_copy_async   cudaMemcpyAsync of `bytes` device bytes on `stream` (peer pointers allowed). */
+typedef struct vk_ipc_handle {
+    uint8_t handle[64]; /* cudaIpcMemHandle_t */
+    uint64_t offset;    /* byte offset of the buffer inside the exported allocation */
+} vk_ipc_handle;
+
+int vk_ipc_export(const void* ptr, vk_ipc_handle* out);
+int vk_ipc_import(const vk_ipc_handle* handle, void** out_ptr);
+int vk_ipc_release(void* ptr);
+int vk_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
 /* Device and library state. */
 int vk_init(int device);                 /* optional: warm per-device state (SM count, attrs) */
 int vk_shutdown(void);                   /* frees per-device state and NCCL communicators    */

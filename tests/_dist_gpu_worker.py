@@ -1,4 +1,5 @@
-"""torchrun worker for tests/test_sharded_gpu.py: one process per GPU, NCCL all-gather of C."""
+"""torchrun worker for tests/test_sharded_gpu.py: one process per GPU, NCCL all-gather of C and the
+copy-engine gather overlapped with the GEMM (dist_gemm.PeerRowGather)."""
 import datetime
 import os
 import sys
@@ -31,6 +32,16 @@ def main():
         g16, _ = v0.v0_f16(A, B)
         c = C.cpu().numpy()
         ok = ok and not np.isnan(c.astype(np.float32)).any() and v0.max_elem_rel(c, g16) <= 2e-3
+        # copy-engine gather overlapped with the GEMM (chunks may take another tail split: tolerance)
+        C2 = torch.full((m, 1536), float("nan"), dtype=torch.float16, device=dev)
+        pg = dist_gemm.PeerRowGather(C2, off, rank)
+        for _ in range(2):  # twice: the second run overwrites a complete buffer
+            pg.run(torch.from_numpy(A[off[rank]:off[rank + 1]]).to(dev), torch.from_numpy(B).to(dev),
+                   lambda a, b, out: vk.gemm(a, b, out), chunks=2)
+        torch.cuda.synchronize(dev)
+        pg.close()
+        c2 = C2.cpu().numpy()
+        ok = ok and not np.isnan(c2.astype(np.float32)).any() and v0.max_elem_rel(c2, g16) <= 2e-3
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     dist.destroy_process_group()

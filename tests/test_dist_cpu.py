@@ -40,6 +40,34 @@ def _worker(rank, world, port, m, n, k, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("rows,chunks", [(2048, 2), (2001, 2), (100, 4), (0, 2), (1000, 3), (4096, 1), (256, 8)])
+def test_chunk_rows_cover_aligned(rows, chunks):
+    from vibekernel_b200 import dist_gemm
+    parts = dist_gemm.chunk_rows(rows, chunks)
+    assert len(parts) <= max(chunks, 1)
+    covered = [r for a, b in parts for r in range(a, b)]
+    assert covered == list(range(rows))
+    assert all(a % 256 == 0 for a, _ in parts)
+
+
+@pytest.mark.parametrize("m,world", [(4096, 2), (2001, 2), (16384, 8), (1000, 3)])
+def test_push_plan_writes_each_rank_rows_to_every_peer(m, world):
+    """Union over ranks of the planned peer copies = every row of C on every rank except the rows the
+    rank computes itself, each exactly once."""
+    from vibekernel_b200 import dist_gemm, row_blocks
+    off = row_blocks(m, world)
+    row_bytes = 3
+    received = {p: [] for p in range(world)}
+    for r in range(world):
+        for (r0, r1), copies in dist_gemm.push_plan(off, r, 2, row_bytes):
+            assert [p for p, _, _ in copies] == [p for p in range(world) if p != r]
+            for p, start, nbytes in copies:
+                assert start == (off[r] + r0) * row_bytes and nbytes == (r1 - r0) * row_bytes
+                received[p].extend(range(start // row_bytes, (start + nbytes) // row_bytes))
+    for p in range(world):
+        assert sorted(received[p]) == [i for i in range(m) if not off[p] <= i < off[p + 1]]
+
+
 @pytest.mark.parametrize("m", [64, 67])  # even split (all-gather) and uneven split (broadcasts)
 def test_two_rank_gloo_sharded_matmul(m):
     ctx = mp.get_context("spawn")

@@ -39,7 +39,8 @@ EXPORTED = (
     "vk_gemm", "vk_matmul_f16", "vk_matmul_f32", "vk_gemm_sharded", "vk_init", "vk_shutdown",
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
     "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
-    "vk_gemm_host", "vk_gemm_ex", "vk_read_trace_cta",
+    "vk_gemm_host", "vk_gemm_ex", "vk_read_trace_cta", "vk_ipc_export", "vk_ipc_import", "vk_ipc_release",
+    "vk_copy_async",
 )
 
 
@@ -78,6 +79,10 @@ class ShardArgs(ctypes.Structure):
         ("dtype", ctypes.c_int32), ("acc", ctypes.c_int32), ("algo", ctypes.c_int32),
         ("allgather_c", ctypes.c_int32), ("times_ms", ctypes.POINTER(ctypes.c_float)),
     ]
+
+
+class IpcHandle(ctypes.Structure):
+    _fields_ = [("handle", ctypes.c_uint8 * 64), ("offset", ctypes.c_uint64)]
 
 
 def _load() -> ctypes.CDLL:
@@ -123,6 +128,14 @@ def _load() -> ctypes.CDLL:
     lib.vk_read_trace.restype = ctypes.c_int
     lib.vk_read_trace_cta.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]
     lib.vk_read_trace_cta.restype = ctypes.c_int
+    lib.vk_ipc_export.argtypes = [ctypes.c_void_p, ctypes.POINTER(IpcHandle)]
+    lib.vk_ipc_export.restype = ctypes.c_int
+    lib.vk_ipc_import.argtypes = [ctypes.POINTER(IpcHandle), ctypes.POINTER(ctypes.c_void_p)]
+    lib.vk_ipc_import.restype = ctypes.c_int
+    lib.vk_ipc_release.argtypes = [ctypes.c_void_p]
+    lib.vk_ipc_release.restype = ctypes.c_int
+    lib.vk_copy_async.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.vk_copy_async.restype = ctypes.c_int
     return lib
 
 
@@ -369,6 +382,31 @@ def gemm_sharded(A_parts, B_parts, C_parts, m: int, n: int, k: int, *, acc: str 
     s.times_ms = times
     check(lib.vk_gemm_sharded(ctypes.byref(s)))
     return float(times[0]), float(times[1])
+
+
+def ipc_export(tensor) -> bytes:
+    """CUDA IPC handle (+ offset) of a device tensor's memory, as bytes to send to a peer process."""
+    h = IpcHandle()
+    check(lib.vk_ipc_export(ctypes.c_void_p(tensor.data_ptr()), ctypes.byref(h)))
+    return bytes(ctypes.string_at(ctypes.addressof(h), ctypes.sizeof(h)))
+
+
+def ipc_import(handle: bytes) -> int:
+    """Maps a buffer exported by ANOTHER process (``ipc_export``) into this one; returns its address."""
+    h = IpcHandle.from_buffer_copy(handle)
+    p = ctypes.c_void_p()
+    check(lib.vk_ipc_import(ctypes.byref(h), ctypes.byref(p)))
+    return int(p.value)
+
+
+def ipc_release(ptr: int) -> None:
+    check(lib.vk_ipc_release(ctypes.c_void_p(ptr)))
+
+
+def copy_async(dst: int, src: int, nbytes: int, stream=None) -> None:
+    """Device-to-device copy of ``nbytes`` (peer addresses allowed) on ``stream`` (copy engines)."""
+    check(lib.vk_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes,
+                            ctypes.c_void_p(stream.cuda_stream if stream is not None else 0)))
 
 
 def row_blocks(m: int, parts: int):

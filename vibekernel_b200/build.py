@@ -17,7 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libvkgemm.so")
-SOURCES = ["vkgemm.cu", "sharded.cu", "host_gemm.cu"]
+SOURCES = ["vkgemm.cu", "sharded.cu", "host_gemm.cu", "peer_ipc.cu"]
 DEPS = SOURCES + ["ptx.cuh", "tc_gemm.cuh", "simt_gemm.cuh", "vk_internal.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -2,8 +2,14 @@
 
 One process per GPU.  Rank r owns rows [off[r], off[r+1]) of A and C (``row_blocks``) and a full
 copy of B; there is no exchange on the data path.  The only collective is the optional
-all-gather of the C row blocks (NCCL over NVLink on B200; gloo in the CPU tests), in place in a
-full [m, n] buffer on every rank: C is row-major, so each rank's block is one contiguous span.
+all-gather of the C row blocks, in place in a full [m, n] buffer on every rank: C is row-major,
+so each rank's block is one contiguous span.  Two ways:
+  * ``allgather_rows``: NCCL (over NVLink on B200; gloo in the CPU tests) after the GEMM;
+  * ``PeerRowGather``: overlapped with the GEMM.  Every rank maps the peers' C buffers into its
+    process once (CUDA IPC), computes its rows in chunks and, as each chunk finishes, pushes it
+    into every peer's C with the copy engines (no SMs taken from the GEMM) while the next chunk
+    is computed; a one-element all-reduce at the end completes on every rank only after every
+    rank's pushes have.
 The reference has no multi-GPU path (README.md:161); this is the layer BASELINE.json asks for.
 """
 from __future__ import annotations
@@ -22,6 +28,85 @@ def allgather_rows(C_full, off, rank: int, group=None) -> None:
         for root in range(world):
             if off[root + 1] > off[root]:
                 dist.broadcast(C_full[off[root]:off[root + 1]], src=root, group=group)
+
+
+def chunk_rows(rows: int, chunks: int, align: int = 256):
+    """Splits a block of ``rows`` rows into at most ``chunks`` pieces [(r0, r1), ...] whose
+    boundaries are multiples of ``align`` rows (one pair tile), the last piece taking the rest."""
+    if rows <= 0:
+        return []
+    step = -(-rows // max(chunks, 1))
+    step = -(-step // align) * align
+    return [(r0, min(r0 + step, rows)) for r0 in range(0, rows, step)]
+
+
+def push_plan(off, rank: int, chunks: int, row_bytes: int):
+    """The copies rank ``rank`` issues after each chunk: [(chunk_rows, [(peer, byte_offset, nbytes), ...])].
+    The byte offset is the same in the local and in every peer's full C buffer."""
+    world = len(off) - 1
+    plan = []
+    for r0, r1 in chunk_rows(off[rank + 1] - off[rank], chunks):
+        start = (off[rank] + r0) * row_bytes
+        plan.append(((r0, r1), [(p, start, (r1 - r0) * row_bytes) for p in range(world) if p != rank]))
+    return plan
+
+
+class PeerRowGather:
+    """Copy-engine all-gather of C row blocks overlapped with the GEMM (one process per GPU).
+
+    Collective: every rank constructs it with the same ``off`` (exchanges IPC handles of the full C
+    buffers), calls ``run`` the same number of times and ``close`` once.  ``C_full`` must be a
+    contiguous [m, n] device tensor that stays allocated until ``close``.
+    """
+
+    def __init__(self, C_full, off, rank: int, group=None):
+        import torch
+        import torch.distributed as dist
+        from . import ipc_export, ipc_import
+        if not C_full.is_contiguous():
+            raise ValueError("C_full must be contiguous")
+        self.C_full, self.off, self.rank, self.group = C_full, list(off), rank, group
+        world = len(off) - 1
+        handles = [None] * world
+        dist.all_gather_object(handles, ipc_export(C_full), group=group)
+        self.peers = {p: ipc_import(handles[p]) for p in range(world) if p != rank}
+        dev = C_full.device
+        self.streams = {p: torch.cuda.Stream(device=dev) for p in self.peers}  # one copy queue per peer
+        self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    def run(self, A_local, B, gemm, chunks: int = 2):
+        """``gemm(A_rows, B, C_rows)`` on each chunk of this rank's rows; each finished chunk is
+        pushed to every peer while the next one is computed.  Returns when (stream order) every
+        rank's C_full is complete."""
+        import torch
+        import torch.distributed as dist
+        from . import copy_async
+        C = self.C_full
+        row_bytes = C.stride(0) * C.element_size()
+        base = C.data_ptr()
+        compute = torch.cuda.current_stream(C.device)
+        for (r0, r1), copies in push_plan(self.off, self.rank, chunks, row_bytes):
+            lo = self.off[self.rank]
+            gemm(A_local[r0:r1], B, C[lo + r0:lo + r1])
+            ev = torch.cuda.Event()
+            ev.record(compute)
+            for p, start, nbytes in copies:
+                self.streams[p].wait_event(ev)
+                copy_async(self.peers[p] + start, base + start, nbytes, self.streams[p])
+        for st in self.streams.values():
+            done = torch.cuda.Event()
+            done.record(st)
+            compute.wait_event(done)
+        dist.all_reduce(self.flag, group=self.group)
+        return C
+
+    def close(self) -> None:
+        import torch
+        from . import ipc_release
+        torch.cuda.synchronize(self.C_full.device)
+        for ptr in self.peers.values():
+            ipc_release(ptr)
+        self.peers = {}
 
 
 def sharded_matmul(A_local, B, C_full, off, rank: int, gemm, allgather: bool = True, group=None):
