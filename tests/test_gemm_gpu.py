@@ -198,22 +198,25 @@ def test_sgemm_ragged(vk, shape):
     assert v0.rel_frobenius(c, g) <= FROB_SGEMM
 
 
-@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1000, 1000, 1000), (300, 200, 20), (129, 260, 36)])
+@pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1000, 1000, 1000), (300, 200, 20), (129, 260, 36),
+                                   (64, 4, 1004), (1, 1, 1)])
 def test_sgemm_paired_fma_bitwise(vk, shape):
     """The paired-FMA SGEMM performs every element's fused multiply-adds in the same order as the
     scalar-FMA kernel: the two results are bitwise equal."""
     m, n, k = shape
     A, B = v0.make_inputs(m, n, k, 33, dist="normal", dtype=np.float32)
     dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
-    paired = vk.gemm(dA, dB)
+    out = {}
     try:
-        vk.set_option("sgemm_paired", 0)
-        scalar = vk.gemm(dA, dB)
+        for variant in (1, 0):
+            vk.set_option("sgemm_paired", variant)
+            out[variant] = vk.gemm(dA, dB)
     finally:
         vk.set_option("sgemm_paired", 1)
     torch.cuda.synchronize()
-    assert torch.equal(paired.view(torch.int32), scalar.view(torch.int32))
-    assert v0.rel_frobenius(paired.cpu().numpy(), v0.v0_f32(A, B)) <= FROB_SGEMM
+    for variant in (1,):
+        assert torch.equal(out[variant].view(torch.int32), out[0].view(torch.int32)), variant
+    assert v0.rel_frobenius(out[1].cpu().numpy(), v0.v0_f32(A, B)) <= FROB_SGEMM
 
 
 @pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1000, 1000, 1000), (300, 200, 20)])

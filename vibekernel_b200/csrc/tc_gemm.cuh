@@ -463,8 +463,12 @@ __global__ void __launch_bounds__(192, 1)
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
                     const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+                    // The last k-block of a ragged K holds zero-filled k-steps: issue only the
+                    // 16-deep MMAs that touch k < K (K = 3000: 4 of 8).
+                    const int kk_end = min(Cfg::kBK / 16, (p.K - kb * Cfg::kBK + 15) / 16);
 #pragma unroll
                     for (int kk = 0; kk < Cfg::kBK / 16; ++kk) {
+                        if (kk >= kk_end) break;
                         const uint64_t a_desc =
                             A_MN ? smem_desc_sw128(a_addr + kk * 16 * 128, kMnLbo, 1024)
                                  : smem_desc_sw128(a_addr + (kk >> 2) * Cfg::kABox + (kk & 3) * 32, 16, 1024);
