@@ -105,8 +105,10 @@ struct DeviceState {
     // by the first vk_gemm_noalloc call made with the device current.
     std::atomic<void*> noalloc_scratch{nullptr};
     int sm_count = 0;
+    // Append-only table; num_kernels is published with release after the new slot is written, so
+    // the lock-free scan in kernel_slot sees only complete slots.
     KernelSlot kernels[kMaxKernels];
-    int num_kernels = 0;
+    std::atomic<int> num_kernels{0};
     // Tail-split scratch, one per stream that launched a split GEMM (launches on different streams
     // may overlap on the GPU, so they must not share partials or counters), allocated on first
     // need: fp32 partials for at most one unit per persistent CTA (sm_count x 128 x 256 floats,
@@ -192,20 +194,22 @@ template <typename Kernel>
 static int kernel_slot(DeviceState& st, Kernel fn, int smem, int threads, int cluster, int* max_units)
 {
     const void* key = reinterpret_cast<const void*>(fn);
-    for (int i = 0; i < st.num_kernels; ++i) {
+    const int seen = st.num_kernels.load(std::memory_order_acquire);
+    for (int i = 0; i < seen; ++i) {
         if (st.kernels[i].fn == key) {
             *max_units = st.kernels[i].max_clusters;
             return VK_OK;
         }
     }
     std::lock_guard<std::mutex> lk(g_mu);
-    for (int i = 0; i < st.num_kernels; ++i) {
+    const int count = st.num_kernels.load(std::memory_order_relaxed);
+    for (int i = 0; i < count; ++i) {
         if (st.kernels[i].fn == key) {
             *max_units = st.kernels[i].max_clusters;
             return VK_OK;
         }
     }
-    if (st.num_kernels >= kMaxKernels) return set_error(VK_ERR_UNSUPPORTED, "kernel table full");
+    if (count >= kMaxKernels) return set_error(VK_ERR_UNSUPPORTED, "kernel table full");
     VK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int units = 0;
     if (cluster > 1) {
@@ -228,10 +232,10 @@ static int kernel_slot(DeviceState& st, Kernel fn, int smem, int threads, int cl
         units = per_sm * st.sm_count;
     }
     if (units <= 0) return set_error(VK_ERR_CUDA, "kernel cannot be resident (smem %d)", smem);
-    KernelSlot& s = st.kernels[st.num_kernels];
+    KernelSlot& s = st.kernels[count];
     s.fn = key;
     s.max_clusters = units;
-    st.num_kernels++;
+    st.num_kernels.store(count + 1, std::memory_order_release);
     *max_units = units;
     return VK_OK;
 }
