@@ -13,7 +13,9 @@
 //   warp 1      TMEM allocator (whole warp) and, in the pair's leader CTA, the MMA issuer (one
 //               lane).  Two accumulators (2 x BN TMEM columns) alternate between tiles, so the
 //               epilogue of tile i overlaps the main loop of tile i+1.
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, convert, store to global.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, fused epilogue, fp16 pack
+//               into swizzled shared staging, TMA tile store of each 32 x 32 box (per-lane
+//               coalesced stores when C cannot take TMA stores).
 //
 // Pair mode (CG = 2): the two CTAs of a cluster each hold 128 rows of A and BN/2 columns of B
 // per stage; the leader issues 256 x BN x 16 MMAs that read both CTAs' shared memory and write
@@ -56,8 +58,9 @@ struct TcParams {
     int vec_ok;              // C / C32 alignment allows 16-byte stores
     int c_tma;               // 1: fp16 C is written by TMA tile stores through the C tensor map
     unsigned long long timeout_ns;
-    // work units: [0, full_units) are whole tiles; then the tail tiles, each cut either into two
-    // column halves (nsplit = 1: BN/2-wide MMAs, no reduction) or into `split` k-slices
+    // work units: full_units whole tiles and the tail tiles, each cut either into two column
+    // halves (nsplit = 1: BN/2-wide MMAs, no reduction) or into `split` k-slices; the whole tiles
+    // come first ([0, full_units)) unless tail_first
     int units, full_units, split, nsplit;
     // tail_first = 1 (k-slices only): the slice units are numbered before the whole tiles, so each
     // cluster runs its slice first and the slice's publish / reduce epilogue overlaps the main loop
