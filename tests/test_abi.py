@@ -79,3 +79,21 @@ def test_no_device_is_an_error_not_a_fallback():
     a.m = a.n = a.k = 8
     rc = vk.lib.vk_gemm(ctypes.byref(a))
     assert rc in (vk.VK_ERR_CUDA, vk.VK_ERR_NO_DEVICE)
+
+
+def test_peer_plumbing_rejects_bad_arguments_without_gpu():
+    """The IPC / peer-copy entry points validate their arguments before any CUDA call."""
+    import vibekernel_b200 as vk
+    lib = vk.lib
+    h = vk.IpcHandle()
+    assert lib.vk_ipc_export(None, ctypes.byref(h)) == vk.VK_ERR_INVALID_ARGUMENT
+    assert lib.vk_ipc_export(ctypes.c_void_p(0x1000), None) == vk.VK_ERR_INVALID_ARGUMENT
+    p = ctypes.c_void_p()
+    assert lib.vk_ipc_import(None, ctypes.byref(p)) == vk.VK_ERR_INVALID_ARGUMENT
+    assert lib.vk_ipc_import(ctypes.byref(h), None) == vk.VK_ERR_INVALID_ARGUMENT
+    # only pointers handed out by vk_ipc_import may be released
+    assert lib.vk_ipc_release(ctypes.c_void_p(0x1000)) == vk.VK_ERR_INVALID_ARGUMENT
+    assert "vk_ipc_import" in vk.last_error()
+    assert lib.vk_copy_async(None, None, 0, None) == vk.VK_OK  # nothing to copy
+    assert lib.vk_copy_async(None, ctypes.c_void_p(0x1000), 16, None) == vk.VK_ERR_INVALID_ARGUMENT
+    assert ctypes.sizeof(vk.IpcHandle) == 72  # 64-byte cudaIpcMemHandle_t + 8-byte offset
