@@ -227,9 +227,10 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *                     tensor-core kernel; 0 = such problems run on the predicated CUDA-core kernel
  *   "sgemm_v2"        1 (default) = fp32 GEMM uses the cp.async pipelined kernel when A and B are
  *                     16-byte aligned with lda, ldb multiples of 4; 0 = always the register-staged one
- *   "sgemm_paired"    1 (default) = that kernel runs its inner product on the paired fp32 FMA of
- *                     sm_100 (two fused multiply-adds per instruction; bitwise the same results);
- *                     0 = scalar FMAs
+ *   "sgemm_paired"    inner product of that kernel: 1 (default) = paired fp32 FMAs of sm_100 (two
+ *                     fused multiply-adds per instruction), 8 x 16 outputs per thread, 128 threads;
+ *                     2 = paired FMAs, 8 x 8 per thread, 256 threads; 0 = scalar FMAs, 8 x 8.  All
+ *                     three give bitwise the same results
  *   "clock_probe"     1 = the tensor-core kernels accumulate the SM cycles and nanoseconds of
  *                     their first CTA (read with vk_read_clock_probe); 0 (default) = off
  *   "trace"           1 = the tensor-core kernels record a launch timeline (vk_read_trace)

@@ -201,20 +201,20 @@ def test_sgemm_ragged(vk, shape):
 @pytest.mark.parametrize("shape", [(4096, 4096, 4096), (1000, 1000, 1000), (300, 200, 20), (129, 260, 36),
                                    (64, 4, 1004), (1, 1, 1)])
 def test_sgemm_paired_fma_bitwise(vk, shape):
-    """The paired-FMA SGEMM performs every element's fused multiply-adds in the same order as the
-    scalar-FMA kernel: the two results are bitwise equal."""
+    """Both paired-FMA SGEMMs (8 x 16 outputs per thread: default; 8 x 8) perform every element's
+    fused multiply-adds in the same order as the scalar-FMA kernel: bitwise equal results."""
     m, n, k = shape
     A, B = v0.make_inputs(m, n, k, 33, dist="normal", dtype=np.float32)
     dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
     out = {}
     try:
-        for variant in (1, 0):
+        for variant in (1, 2, 0):
             vk.set_option("sgemm_paired", variant)
             out[variant] = vk.gemm(dA, dB)
     finally:
         vk.set_option("sgemm_paired", 1)
     torch.cuda.synchronize()
-    for variant in (1,):
+    for variant in (1, 2):
         assert torch.equal(out[variant].view(torch.int32), out[0].view(torch.int32)), variant
     assert v0.rel_frobenius(out[1].cpu().numpy(), v0.v0_f32(A, B)) <= FROB_SGEMM
 

@@ -1,5 +1,6 @@
 // CUDA-core kernels:
-//   * sgemm_ffma_v2_kernel -- the default fp32 SGEMM (cp.async 3-stage pipeline, below);
+//   * sgemm_ffma_w16_kernel -- the default fp32 SGEMM (cp.async 3-stage pipeline, paired FMAs,
+//     8 x 16 outputs per thread, below), and sgemm_ffma_v2_kernel, its 8 x 8 sibling;
 //   * sgemm_ffma_kernel  -- fp32 SGEMM for operands the v2 kernel's 16-byte copies cannot take
 //     (the reference has only a cBLAS v0 and a library call for
 //     fp32: results/naive/src/matmul_f32/matmul_f32_v0_cblas.cpp:8-12,
@@ -7,7 +8,8 @@
 //     8 x 8 outputs per thread in four 4 x 4 quadrants, 128-bit global loads, A staged
 //     transposed, shared-memory double buffering with register prefetch of the next k-slab.
 //   * hgemm_simt_kernel  -- fp16 in, fp32 accumulate, any strides and alignment (the fallback for
-//     shapes the TMA path cannot describe: row pitch not a multiple of 16 bytes).
+//     operands the TMA path cannot describe -- row pitch not a multiple of 16 bytes -- when they
+//     are not repacked).
 //   * fill_zero_kernel   -- C = 0 for k == 0.
 #pragma once
 
@@ -171,8 +173,9 @@ __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_kernel(const SgemmPa
 }
 
 // ---------------------------------------------------------------------------------------------
-// sgemm_ffma_v2_kernel -- the default fp32 SGEMM for 16-byte-aligned A/B with lda, ldb multiples
-// of 4 (inner product on the paired FMA by default, see PAIRED below).  128 x 128 CTA tile, BK = 16, 256 threads, 8 x 8 outputs per thread in four 4 x 4
+// sgemm_ffma_v2_kernel -- fp32 SGEMM for 16-byte-aligned A/B with lda, ldb multiples of 4, 8 x 8
+// outputs per thread (scalar or paired FMAs, see PAIRED below); the default for such operands is
+// sgemm_ffma_w16_kernel further down, which shares this kernel's ring and shared layout.  128 x 128 CTA tile, BK = 16, 256 threads, 8 x 8 outputs per thread in four 4 x 4
 // quadrants.  Operands move global -> shared with cp.async (16-byte, zero-filled at the edges) in a
 // 3-stage ring, so no registers stage the next tile and three k-tiles are in flight.  A stays
 // K-contiguous in shared memory (rows padded to 20 floats so the two rows a warp reads per
@@ -317,6 +320,120 @@ __global__ void __launch_bounds__(kSgThreads, 2) sgemm_ffma_v2_kernel(const Sgem
             const int col = n0 + tx * 4 + h * 64;
             if (col < p.N)
                 sg_store4(p, row, col, acc[i][4 * h + 0], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// sgemm_ffma_w16_kernel -- the paired-FMA SGEMM with 16 output columns per thread: 128 x 128 CTA
+// tile, 128 threads (8 rows x 16 columns each: rows ty*4 + 0..3 and 64 + ty*4 + 0..3, columns
+// tx*4 + 0..3 + {0, 32, 64, 96}), BK = 16, the same 3-stage cp.async ring and shared layout as
+// sgemm_ffma_v2_kernel.  Per k a thread loads 8 A values (broadcast into pairs) and 16 B values for
+// 64 paired FMAs, half the non-FMA instructions per FMA of the 8 x 8 thread tile.  Every output
+// element gets the same fused multiply-adds in the same k order, so results are bitwise those of
+// the other SGEMM kernels.
+constexpr int kSgW16Threads = 128;
+
+__device__ __forceinline__ void sgw16_load_stage(const SgemmParams& p, float* As, float* Bs, int m0, int n0, int k0)
+{
+    const int t = threadIdx.x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        // A: 128 rows x 16 k = 512 float4, four per row
+        const int f = t + i * kSgW16Threads;
+        const int row = f >> 2, kq = (f & 3) * 4;
+        const int gr = m0 + row, gk = k0 + kq;
+        int bytes = 0;
+        const float* src = p.A;
+        if (gr < p.M && gk < p.K) {
+            bytes = min(4, p.K - gk) * 4;
+            src = p.A + static_cast<long long>(gr) * p.lda + gk;
+        }
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(As + row * kSg2APitch + kq)), src, bytes);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        // B: 16 k-rows x 128 columns = 512 float4, 32 per row
+        const int f = t + i * kSgW16Threads;
+        const int row = f >> 5, cq = (f & 31) * 4;
+        const int gk = k0 + row, gc = n0 + cq;
+        int bytes = 0;
+        const float* src = p.B;
+        if (gk < p.K && gc < p.N) {
+            bytes = min(4, p.N - gc) * 4;
+            src = p.B + static_cast<long long>(gk) * p.ldb + gc;
+        }
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(Bs + row * kSgBN + cq)), src, bytes);
+    }
+}
+
+__global__ void __launch_bounds__(kSgW16Threads, 2) sgemm_ffma_w16_kernel(const SgemmParams p)
+{
+    extern __shared__ __align__(16) float sgw_smem[];
+    float* As = sgw_smem;                             // [stage][128][20]
+    float* Bs = sgw_smem + kSg2Stages * kSg2AFloats;  // [stage][16][128]
+    const int t = threadIdx.x;
+    const int tx = t & 7, ty = t >> 3;
+    const int m0 = blockIdx.y * kSgBM, n0 = blockIdx.x * kSgBN;
+    const int nk = (p.K + kSg2BK - 1) / kSg2BK;
+
+    float2 acc2[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc2[i][j] = make_float2(0.f, 0.f);
+
+#pragma unroll
+    for (int s = 0; s < kSg2Stages - 1; ++s) {
+        if (s < nk) sgw16_load_stage(p, As + s * kSg2AFloats, Bs + s * kSg2BFloats, m0, n0, s * kSg2BK);
+        cp_async_commit();
+    }
+    for (int kt = 0; kt < nk; ++kt) {
+        cp_async_wait<kSg2Stages - 2>();
+        __syncthreads();  // stage kt landed for all threads; stage kt-1 is free for the next load
+        const int nxt = kt + kSg2Stages - 1;
+        if (nxt < nk)
+            sgw16_load_stage(p, As + (nxt % kSg2Stages) * kSg2AFloats, Bs + (nxt % kSg2Stages) * kSg2BFloats, m0, n0,
+                             nxt * kSg2BK);
+        cp_async_commit();
+        const float* a_s = As + (kt % kSg2Stages) * kSg2AFloats;
+        const float* b_s = Bs + (kt % kSg2Stages) * kSg2BFloats;
+#pragma unroll
+        for (int kc = 0; kc < kSg2BK; kc += 4) {
+            float4 a4[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                a4[i] = *reinterpret_cast<const float4*>(a_s + (ty * 4 + (i & 3) + (i >> 2) * 64) * kSg2APitch + kc);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                float2 bp[8];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const float4 b = *reinterpret_cast<const float4*>(b_s + (kc + kk) * kSgBN + tx * 4 + h * 32);
+                    bp[2 * h] = make_float2(b.x, b.y);
+                    bp[2 * h + 1] = make_float2(b.z, b.w);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float av = kk == 0 ? a4[i].x : kk == 1 ? a4[i].y : kk == 2 ? a4[i].z : a4[i].w;
+                    const float2 ap = make_float2(av, av);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc2[i][j] = __ffma2_rn(ap, bp[j], acc2[i][j]);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int row = m0 + ty * 4 + (i & 3) + (i >> 2) * 64;
+        if (row >= p.M) continue;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const int col = n0 + tx * 4 + h * 32;
+            if (col < p.N)
+                sg_store4(p, row, col, acc2[i][2 * h].x, acc2[i][2 * h].y, acc2[i][2 * h + 1].x, acc2[i][2 * h + 1].y);
         }
     }
 }

@@ -598,20 +598,24 @@ static int launch_sgemm(const Problem& pb)
     dim3 grid(static_cast<unsigned>((pb.n + kSgBN - 1) / kSgBN), static_cast<unsigned>((pb.m + kSgBM - 1) / kSgBM));
     if (grid.y > 65535u) return set_error(VK_ERR_UNSUPPORTED, "m too large for the SGEMM grid");
     if (p.vec_a && p.vec_b && g_sgemm_v2.load(std::memory_order_relaxed)) {
-        // smem attribute set once per device (bit per ordinal < 31) and kernel.  A variant that stored
+        // smem attribute set once per device (bit per ordinal < 31) and kernel.  Variants (all bitwise
+        // equal): 1 (default) = paired FMAs, 8 x 16 outputs per thread (55.9 TFLOP/s at 4096^3 on B200);
+        // 2 = paired FMAs, 8 x 8 per thread (49.8); 0 = scalar FMAs, 8 x 8 (42.2).  A variant that stored
         // the A tile pre-broadcast as (a, a) pairs (register-staged A) measured 10 % slower than the
-        // register broadcast below at 4096^3 and was dropped.
-        static std::atomic<int> attr_dev_mask[2] = {{0}, {0}};
-        const int paired = g_sgemm_paired.load(std::memory_order_relaxed) != 0 ? 1 : 0;
-        auto fn = paired ? sgemm_ffma_v2_kernel<true> : sgemm_ffma_v2_kernel<false>;
+        // register broadcast and was dropped.
+        static std::atomic<int> attr_dev_mask[3] = {{0}, {0}, {0}};
+        const int variant = g_sgemm_paired.load(std::memory_order_relaxed);
+        auto fn = variant == 1 ? sgemm_ffma_w16_kernel
+                               : (variant == 2 ? sgemm_ffma_v2_kernel<true> : sgemm_ffma_v2_kernel<false>);
+        const int threads = variant == 1 ? kSgW16Threads : kSgThreads;
         int dev = 0;
         VK_CUDA_TRY(cudaGetDevice(&dev));
         const int bit = 1 << (dev & 31);
-        if (!(attr_dev_mask[paired].load() & bit)) {
+        if (!(attr_dev_mask[variant].load() & bit)) {
             VK_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSg2SmemBytes));
-            attr_dev_mask[paired].fetch_or(bit);
+            attr_dev_mask[variant].fetch_or(bit);
         }
-        fn<<<grid, kSgThreads, kSg2SmemBytes, pb.stream>>>(p);
+        fn<<<grid, threads, kSg2SmemBytes, pb.stream>>>(p);
     } else {
         sgemm_ffma_kernel<<<grid, kSgThreads, 0, pb.stream>>>(p);
     }
@@ -1037,7 +1041,8 @@ extern "C" int vk_set_option(const char* name, int64_t value)
         return VK_OK;
     }
     if (strcmp(name, "sgemm_paired") == 0) {
-        g_sgemm_paired.store(value != 0 ? 1 : 0);
+        if (value < 0 || value > 2) return set_error(VK_ERR_INVALID_ARGUMENT, "sgemm_paired must be 0, 1 or 2");
+        g_sgemm_paired.store(static_cast<int>(value));
         return VK_OK;
     }
     if (strcmp(name, "trace") == 0) {
