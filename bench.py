@@ -399,7 +399,7 @@ def main():
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernel, from
 # the ncu captures summarised in profiles/tc_gemm_pair_rubric4096.md and profiles/sgemm_ffma_4096.md;
 # None where no capture of the current kernel exists.
-TRAFFIC = {"rubric": 136087296, "ragged": 116693248, "sgemm": 593867776}
+TRAFFIC = {"rubric": 136087296, "ragged": 116693248, "sgemm": 568920064}
 
 if __name__ == "__main__":
     main()
