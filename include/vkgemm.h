@@ -237,6 +237,16 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  * Returns VK_ERR_INVALID_ARGUMENT for an unknown name or value. */
 int vk_set_option(const char* name, int64_t value);
 
+/* Test hook (no counterpart in the reference; touches no device): the work decomposition the
+ * persistent tensor-core kernels would use for `tiles` output tiles of `num_kb` k-blocks on
+ * `max_units` co-resident clusters, from the same planner and unit decoder as the launches.
+ * flags: 1 = tail split allowed, 2 = column halves allowed, 4 = slices-first allowed (also needs
+ * k >= 2560).  out_plan[6] = {units, whole tiles, k-slices per tail tile, column halves (0/1),
+ * slices first (0/1), clusters launched}; out_units (optional, 4 ints per unit, room for
+ * max_units_out units) = {tile, first k-block, end k-block, slice index | 100 + column half | -1}. */
+int vk_debug_schedule(int64_t tiles, int32_t num_kb, int32_t max_units, int64_t k, int32_t flags,
+                      int32_t* out_plan, int32_t* out_units, int32_t max_units_out);
+
 /* Clock probe (no counterpart in the reference, whose scores were confounded by the unlogged
  * SM clock, README.md:160): out3 = {SM cycles, nanoseconds, launches} accumulated since the last
  * clear; cycles / ns is the SM clock in GHz that the kernels actually ran at.  Synchronises. */

@@ -40,7 +40,7 @@ EXPORTED = (
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
     "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
     "vk_gemm_host", "vk_gemm_ex", "vk_read_trace_cta", "vk_ipc_export", "vk_ipc_import", "vk_ipc_release",
-    "vk_copy_async",
+    "vk_copy_async", "vk_debug_schedule",
 )
 
 
@@ -136,6 +136,10 @@ def _load() -> ctypes.CDLL:
     lib.vk_ipc_release.restype = ctypes.c_int
     lib.vk_copy_async.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     lib.vk_copy_async.restype = ctypes.c_int
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    lib.vk_debug_schedule.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
+                                      i32p, i32p, ctypes.c_int32]
+    lib.vk_debug_schedule.restype = ctypes.c_int
     return lib
 
 
@@ -407,6 +411,20 @@ def copy_async(dst: int, src: int, nbytes: int, stream=None) -> None:
     """Device-to-device copy of ``nbytes`` (peer addresses allowed) on ``stream`` (copy engines)."""
     check(lib.vk_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes,
                             ctypes.c_void_p(stream.cuda_stream if stream is not None else 0)))
+
+
+def debug_schedule(tiles: int, num_kb: int, max_units: int, k: int, split: bool = True, nsplit: bool = True,
+                   first: bool = True):
+    """The persistent kernels' work units for a problem (host-side, no device): (plan dict, units list of
+    (tile, kb0, kb1, tag)) with tag = slice index, 100 + column half, or -1 for a whole tile."""
+    plan = (ctypes.c_int32 * 6)()
+    flags = (1 if split else 0) | (2 if nsplit else 0) | (4 if first else 0)
+    check(lib.vk_debug_schedule(tiles, num_kb, max_units, k, flags, plan, None, 0))
+    n = int(plan[0])
+    units = (ctypes.c_int32 * max(4 * n, 1))()
+    check(lib.vk_debug_schedule(tiles, num_kb, max_units, k, flags, plan, units, n))
+    keys = ("units", "full_units", "split", "nsplit", "tail_first", "grid_units")
+    return dict(zip(keys, (int(x) for x in plan))), [tuple(int(units[4 * u + j]) for j in range(4)) for u in range(n)]
 
 
 def row_blocks(m: int, parts: int):

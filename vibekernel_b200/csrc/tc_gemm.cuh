@@ -88,7 +88,7 @@ struct Unit {
     int half;   // column half (0/1) of an n-split tail tile, -1 for the full width
 };
 
-__device__ __forceinline__ Unit unit_info(const TcParams& p, int u)
+__host__ __device__ __forceinline__ Unit unit_info(const TcParams& p, int u)
 {
     Unit w;
     w.half = -1;

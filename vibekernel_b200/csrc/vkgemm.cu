@@ -1003,6 +1003,43 @@ extern "C" const char* vk_last_error_string(void) { return t_last_error.c_str();
 
 extern "C" const char* vk_version_string(void) { return "vkgemm 0.1.0 (sm_100a)"; }
 
+// Test hook: the persistent kernels' work decomposition for a problem, computed on the host by the same
+// planner (plan_schedule) and unit decoder (unit_info) the launches use, so CPU tests can check that
+// every (tile, k-block) is covered exactly once.  No device is touched.
+extern "C" int vk_debug_schedule(int64_t tiles, int32_t num_kb, int32_t max_units, int64_t k, int32_t flags,
+                                 int32_t* out_plan, int32_t* out_units, int32_t max_units_out)
+{
+    if (tiles < 0 || num_kb < 1 || max_units < 1 || out_plan == nullptr)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_debug_schedule: bad arguments");
+    const bool first = (flags & 4) != 0 && k >= kFirstMinK;
+    const Schedule sc = plan_schedule(tiles, num_kb, max_units, (flags & 1) != 0, (flags & 2) != 0, first);
+    out_plan[0] = sc.units;
+    out_plan[1] = sc.full_units;
+    out_plan[2] = sc.split;
+    out_plan[3] = sc.nsplit;
+    out_plan[4] = sc.tail_first;
+    out_plan[5] = sc.grid_units;
+    if (out_units == nullptr) return VK_OK;
+    if (sc.units > max_units_out)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "vk_debug_schedule: %d units, room for %d", sc.units, max_units_out);
+    TcParams p;
+    memset(&p, 0, sizeof(p));
+    p.num_kb = num_kb;
+    p.units = sc.units;
+    p.full_units = sc.full_units;
+    p.split = sc.split;
+    p.nsplit = sc.nsplit;
+    p.tail_first = sc.tail_first;
+    for (int u = 0; u < sc.units; ++u) {
+        const Unit w = unit_info(p, u);
+        out_units[4 * u + 0] = w.tile;
+        out_units[4 * u + 1] = w.kb0;
+        out_units[4 * u + 2] = w.kb1;
+        out_units[4 * u + 3] = w.slice >= 0 ? w.slice : (w.half >= 0 ? 100 + w.half : -1);
+    }
+    return VK_OK;
+}
+
 extern "C" int vk_set_option(const char* name, int64_t value)
 {
     if (name == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_set_option: name is NULL");
