@@ -65,6 +65,18 @@ def _check_f32acc(c16, c32, A, B, gold=None, rows=None):
 TC_VARIANTS = [("tc2", 256), ("tc2", 128), ("tc1", 256), ("tc1", 128)]
 
 
+def test_device_is_sm100_and_library_loaded(vk):
+    """The library is built for sm_100a only: the GPU under test is compute capability 10.0, and the
+    library's own entry point (not a torch fallback) computes C."""
+    assert torch.cuda.get_device_capability(0) == (10, 0)
+    assert vk.lib.vk_init(0) == vk.VK_OK
+    A = torch.ones((256, 64), dtype=torch.float16, device="cuda")
+    B = torch.ones((64, 256), dtype=torch.float16, device="cuda")
+    C = vk.gemm(A, B)
+    torch.cuda.synchronize()
+    assert bool((C == 64).all())
+
+
 @pytest.mark.parametrize("algo,tile_n", TC_VARIANTS + [("simt", 0)])
 def test_cfg0_1024_seed0_fp32acc(vk, algo, tile_n):
     z, A, B = _golden("cfg0_1024_seed0")
