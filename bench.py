@@ -196,9 +196,10 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rubric")
     ap.add_argument("--algo", default="auto")
     ap.add_argument("--tile-n", type=int, default=0)
-    ap.add_argument("--allgather", nargs="?", const="nccl", default=None, choices=["nccl", "pipelined"],
+    ap.add_argument("--allgather", nargs="?", const="nccl", default=None, choices=["nccl", "pipelined", "fused"],
                     help="all-gather C on every rank: nccl = NCCL after the GEMM (default when given); "
-                         "pipelined = copy-engine peer pushes of finished row chunks overlapped with the GEMM")
+                         "pipelined = copy-engine peer pushes of finished row chunks overlapped with the GEMM; "
+                         "fused = the GEMM epilogue stores every C box into the peers' C as well")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -249,18 +250,18 @@ def main():
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def local_gemm(a, b, out):
-        vk.gemm(a, b, out, acc=acc, algo=args.algo, tile_n=args.tile_n, stream=stream)
+    def local_gemm(a, b, out, peers=None):
+        vk.gemm(a, b, out, acc=acc, algo=args.algo, tile_n=args.tile_n, stream=stream, peers=peers)
 
     peer_gather = None
     launches_per_step = 1
-    if C_full is not None and args.allgather == "pipelined":
+    if C_full is not None and args.allgather in ("pipelined", "fused"):
         peer_gather = dist_gemm.PeerRowGather(C_full, off, rank)
-        launches_per_step = len(dist_gemm.chunk_rows(rows, 2))
+        launches_per_step = len(dist_gemm.chunk_rows(rows, 2)) if args.allgather == "pipelined" else 1
 
     def step():
         if peer_gather is not None:
-            peer_gather.run(A, B, local_gemm, chunks=2)  # GEMM chunks + overlapped peer pushes
+            peer_gather.run(A, B, local_gemm, chunks=2, mode=args.allgather)  # GEMM + overlapped peer stores
         else:
             local_gemm(A, B, C)
 

@@ -105,6 +105,15 @@ typedef struct vk_gemm_ext {
 /* vk_gemm with the extensions above; ext == NULL is exactly vk_gemm. */
 int vk_gemm_ex(const vk_gemm_args* args, const vk_gemm_ext* ext);
 
+/* Fused compute + all-gather (no counterpart in the reference): vk_gemm for the fp16 tensor-core
+ * kernels that also stores every finished box of C, at the same row / column offsets and with the
+ * same ldc, into each of the npeers (0..7) buffers peer_C[i] -- typically the matching rows of the
+ * other GPUs' full C, mapped with peer access (one process) or vk_ipc_import (one process per GPU).
+ * The peer stores are plain 16-byte stores over NVLink issued by the epilogue while the main loop
+ * runs on (no TMA on peer memory).  The caller orders the peers' reads after this kernel (an event
+ * or a collective).  fp16 only; operands that would need the predicated kernel are rejected. */
+int vk_gemm_peers(const vk_gemm_args* args, void* const* peer_C, int32_t npeers);
+
 /* No counterpart in the reference.  Same contract as vk_gemm for the fp16 tensor-core kernels
  * (algo AUTO, TC_2SM or TC_1SM; 16-byte aligned A/B with lda, ldb multiples of 8), for callers
  * that cannot allocate device memory: code running during CUDA graph capture, applications whose
@@ -161,7 +170,9 @@ typedef struct vk_shard_args {
     int32_t allgather_c;      /* 0 = local row block only; 1 = NCCL all-gather after the GEMMs;
                                  2 = pipelined: each GPU computes its rows in two chunks and pushes
                                  every finished chunk to all peers with peer-to-peer copies (copy
-                                 engines over NVLink) while the next chunk is computed */
+                                 engines over NVLink) while the next chunk is computed;
+                                 3 = fused: each GPU's epilogue stores every finished box of C into
+                                 all peers' C as well (vk_gemm_peers; fp16, at most 8 GPUs) */
     float* times_ms;          /* optional, length 2: [0] compute max over GPUs, [1] all-gather */
 } vk_shard_args;
 

@@ -42,6 +42,16 @@ def main():
         pg.close()
         c2 = C2.cpu().numpy()
         ok = ok and not np.isnan(c2.astype(np.float32)).any() and v0.max_elem_rel(c2, g16) <= 2e-3
+        # fused: the GEMM epilogue stores into the peers' C itself (same kernel plan as the NCCL run)
+        C3 = torch.full((m, 1536), float("nan"), dtype=torch.float16, device=dev)
+        pg = dist_gemm.PeerRowGather(C3, off, rank)
+        for _ in range(2):
+            pg.run(torch.from_numpy(A[off[rank]:off[rank + 1]]).to(dev), torch.from_numpy(B).to(dev),
+                   lambda a, b, out, peers=None: vk.gemm(a, b, out, peers=peers), mode="fused")
+        torch.cuda.synchronize(dev)
+        pg.close()
+        c3 = C3.cpu().numpy()
+        ok = ok and np.array_equal(c3.view(np.uint16), c.view(np.uint16))
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     dist.destroy_process_group()

@@ -99,3 +99,17 @@ def test_peer_plumbing_rejects_bad_arguments_without_gpu():
     assert lib.vk_copy_async(None, None, 0, None) == vk.VK_OK  # nothing to copy
     assert lib.vk_copy_async(None, ctypes.c_void_p(0x1000), 16, None) == vk.VK_ERR_INVALID_ARGUMENT
     assert ctypes.sizeof(vk.IpcHandle) == 72  # 64-byte cudaIpcMemHandle_t + 8-byte offset
+
+
+def test_peer_gemm_rejects_bad_arguments_without_gpu():
+    import vibekernel_b200 as vk
+    a = vk.GemmArgs()
+    a.m = a.n = a.k = 8
+    a.A = a.B = a.C = 0x1000
+    peers = (ctypes.c_void_p * 8)(*([0x2000] * 8))
+    assert vk.lib.vk_gemm_peers(ctypes.byref(a), peers, 8) == vk.VK_ERR_INVALID_ARGUMENT  # at most 7 peers
+    assert vk.lib.vk_gemm_peers(ctypes.byref(a), None, 1) == vk.VK_ERR_INVALID_ARGUMENT
+    nul = (ctypes.c_void_p * 2)(0x2000, None)
+    assert vk.lib.vk_gemm_peers(ctypes.byref(a), nul, 2) == vk.VK_ERR_INVALID_ARGUMENT
+    a.dtype = vk.DTYPE_F32
+    assert vk.lib.vk_gemm_peers(ctypes.byref(a), peers, 1) == vk.VK_ERR_UNSUPPORTED

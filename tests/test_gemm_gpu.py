@@ -470,3 +470,50 @@ def test_bounded_wait_selftest(vk):
     A, B = v0.make_inputs(256, 256, 256, 81)
     c16, c32 = _run16(vk, A, B)
     _check_f32acc(c16, c32, A, B)
+
+
+@pytest.mark.parametrize("opts", [{}, {"tma_store": 0}], ids=["tma-store", "lane-stores"])
+@pytest.mark.parametrize("shape,acc", [((4096, 4096, 4096), "f32"), ((1000, 19000, 1000), "f32"),
+                                       ((4000, 5120, 3000), "f32"), ((300, 264, 136), "f32"),
+                                       ((4096, 4096, 1024), "f16"), ((1024, 1024, 8192), "f32")])
+def test_peer_stores_copy_every_box(vk, shape, acc, opts):
+    """vk_gemm_peers with a second buffer on the same device standing in for a peer GPU's C: the
+    epilogue's box-by-box copy (whole tiles, k-slice reductions, column halves, ragged edges, TMA and
+    per-lane store paths) lands exactly what the local C gets, and nothing outside the rows / columns
+    of C is touched in either buffer."""
+    m, n, k = shape
+    A, B = v0.make_inputs(m, n, k, 71, lo=-0.5, hi=0.5)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    pad = 24
+    bufs = [torch.full((m + 2, n + pad), 5.0, dtype=torch.float16, device="cuda") for _ in range(2)]
+    C, P = bufs[0][1:m + 1, 8:8 + n], bufs[1][1:m + 1, 8:8 + n]
+    try:
+        for name, val in opts.items():
+            vk.set_option(name, val)
+        vk.gemm(dA, dB, C, acc=acc, peers=[P.data_ptr()])
+        torch.cuda.synchronize()
+    finally:
+        vk.set_option("tma_store", 1)
+    assert torch.equal(C.view(torch.int16), P.view(torch.int16))
+    for b in bufs:
+        out = b.cpu().numpy().astype(np.float32)
+        mask = np.ones_like(out, dtype=bool)
+        mask[1:m + 1, 8:8 + n] = False
+        assert np.all(out[mask] == 5.0), "write outside C"
+    g32 = v0.v0_f16(A, B)[1]
+    c = C.cpu().numpy().astype(np.float32)
+    if acc == "f32":
+        assert v0.max_elem_rel(c, g32) <= ELEM + 2 ** -10
+    else:
+        assert v0.rel_frobenius(c, g32) <= FROB_F16ACC
+    assert vk.device_error(0) == 0
+
+
+def test_peer_stores_reject_paths_without_them(vk):
+    A = torch.ones((64, 64), dtype=torch.float16, device="cuda")
+    B = torch.ones((64, 64), dtype=torch.float16, device="cuda")
+    P = torch.empty((64, 64), dtype=torch.float16, device="cuda")
+    with pytest.raises(vk.VkError):
+        vk.gemm(A, B, algo="simt", peers=[P])
+    with pytest.raises(vk.VkError):
+        vk.gemm(A[:, :0], B[:0], peers=[P])  # k == 0

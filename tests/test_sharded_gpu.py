@@ -47,7 +47,7 @@ def test_sharded_single_gpu_no_exchange(vk):
 
 
 @pytest.mark.parametrize("m", [4096, 4001])  # even split (ncclAllGather) / uneven (broadcasts)
-@pytest.mark.parametrize("mode", [True, "pipelined"], ids=["nccl", "pipelined"])
+@pytest.mark.parametrize("mode", [True, "pipelined", "fused"], ids=["nccl", "pipelined", "fused"])
 def test_sharded_multi_gpu_allgather(vk, m, mode):
     ngpu = torch.cuda.device_count()
     if ngpu < 2:

@@ -40,7 +40,7 @@ EXPORTED = (
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
     "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
     "vk_gemm_host", "vk_gemm_ex", "vk_read_trace_cta", "vk_ipc_export", "vk_ipc_import", "vk_ipc_release",
-    "vk_copy_async", "vk_debug_schedule",
+    "vk_copy_async", "vk_debug_schedule", "vk_gemm_peers",
 )
 
 
@@ -99,6 +99,8 @@ def _load() -> ctypes.CDLL:
     lib.vk_gemm_host.restype = ctypes.c_int
     lib.vk_gemm_ex.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(GemmExt)]
     lib.vk_gemm_ex.restype = ctypes.c_int
+    lib.vk_gemm_peers.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32]
+    lib.vk_gemm_peers.restype = ctypes.c_int
     sz = ctypes.c_size_t
     lib.vk_matmul_f16.argtypes = [ctypes.c_int, sz, sz, sz, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.vk_matmul_f16.restype = ctypes.c_int
@@ -183,14 +185,16 @@ def _row_pitch(t) -> int:
 def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile_n: int = 0,
          stream=None, lda: int = 0, ldb: int = 0, ldc: int = 0, m: int | None = None,
          n: int | None = None, k: int | None = None, trans_a: bool = False, trans_b: bool = False,
-         alpha: float = 1.0, beta: float = 0.0, c_in=None, bias=None, act: str | None = None):
+         alpha: float = 1.0, beta: float = 0.0, c_in=None, bias=None, act: str | None = None, peers=None):
     """C = act(alpha * op(A) @ op(B) + beta * c_in + bias) on the GPU (``vk_gemm`` / ``vk_gemm_ex``).
 
     A is [m, k] (or [k, m] with ``trans_a``) and B is [k, n] (or [n, k] with ``trans_b``), CUDA
     tensors (fp16, or fp32 for the FFMA kernel) with unit column stride; a row stride larger than
     the row length is passed on as lda/ldb.  Returns C (allocated if not given).  ``c_f32``:
     optional fp32 [m, n] tensor receiving the result before rounding (fp16 only).  ``act``: None
-    or "relu".  Asynchronous on ``stream`` (default: torch's current stream).
+    or "relu".  Asynchronous on ``stream`` (default: torch's current stream).  ``peers``: addresses (ints)
+    or tensors of up to 7 peer buffers that also receive C, box by box, at the same row / column offsets
+    and ldc (``vk_gemm_peers``: the fused all-gather; fp16 tensor-core path, no epilogue extensions).
     """
     import torch
     if A.dtype not in (torch.float16, torch.float32) or B.dtype != A.dtype:
@@ -223,6 +227,12 @@ def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile
     a.stream = _stream_handle(stream)
     extended = trans_a or trans_b or alpha != 1.0 or beta != 0.0 or bias is not None or act is not None
     with torch.cuda.device(A.device):
+        if peers is not None and len(peers) > 0:
+            if extended:
+                raise ValueError("peers cannot be combined with transposes or the fused epilogue")
+            addrs = (ctypes.c_void_p * len(peers))(*[p if isinstance(p, int) else p.data_ptr() for p in peers])
+            check(lib.vk_gemm_peers(ctypes.byref(a), addrs, len(peers)))
+            return C
         if not extended:
             check(lib.vk_gemm(ctypes.byref(a)))
             return C
@@ -363,9 +373,9 @@ def gemm_sharded(A_parts, B_parts, C_parts, m: int, n: int, k: int, *, acc: str 
     """Single-process multi-GPU row-block GEMM through ``vk_gemm_sharded``.
 
     A_parts[r]: GPU r's row slice [rows_r, k]; B_parts[r]: full [k, n] on GPU r; C_parts[r]: full
-    [m, n] buffer on GPU r.  ``allgather``: False, True (NCCL after the GEMMs) or "pipelined" (peer
-    copies of finished row chunks overlapped with the GEMM).  Returns (compute_ms, gather_ms), each
-    the max over GPUs.
+    [m, n] buffer on GPU r.  ``allgather``: False, True (NCCL after the GEMMs), "pipelined" (peer
+    copies of finished row chunks overlapped with the GEMM) or "fused" (every GPU's epilogue also
+    stores its C boxes into all peers' C).  Returns (compute_ms, gather_ms), each the max over GPUs.
     """
     import torch
     g = len(A_parts)
@@ -382,7 +392,7 @@ def gemm_sharded(A_parts, B_parts, C_parts, m: int, n: int, k: int, *, acc: str 
     s.dtype = DTYPE_F16 if A_parts[0].dtype == torch.float16 else DTYPE_F32
     s.acc = _ACCS[acc]
     s.algo = _ALGOS[algo]
-    s.allgather_c = 2 if allgather == "pipelined" else (1 if allgather else 0)
+    s.allgather_c = {"pipelined": 2, "fused": 3}.get(allgather, 1 if allgather else 0)
     s.times_ms = times
     check(lib.vk_gemm_sharded(ctypes.byref(s)))
     return float(times[0]), float(times[1])

@@ -176,13 +176,19 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
         cudaSetDevice(prev);
         return rc;
     }
-    if (a->allgather_c < 0 || a->allgather_c > 2) {
+    if (a->allgather_c < 0 || a->allgather_c > 3) {
         cudaSetDevice(prev);
-        return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: allgather_c must be 0, 1 or 2");
+        return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: allgather_c must be 0, 1, 2 or 3");
     }
     const bool pipelined = a->allgather_c == 2 && n_gpu > 1;
     const bool gather = a->allgather_c == 1 && n_gpu > 1;
-    if (pipelined) {
+    const bool fused = a->allgather_c == 3 && n_gpu > 1;
+    if (fused && (n_gpu - 1 > vk::kMaxPeers || a->dtype != VK_DTYPE_F16)) {
+        cudaSetDevice(prev);
+        return vk::set_error(VK_ERR_UNSUPPORTED, "vk_gemm_sharded: the fused gather takes fp16 and at most %d GPUs",
+                             vk::kMaxPeers + 1);
+    }
+    if (pipelined || fused) {
         rc = ensure_peer(g);
         if (rc != VK_OK) {
             cudaSetDevice(prev);
@@ -226,7 +232,18 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
             ga.acc = a->acc;
             ga.algo = a->algo;
             ga.stream = g->streams[r];
-            rc = vk_gemm(&ga);
+            if (fused) {
+                // fused gather: the epilogue also stores every finished box into the same rows of
+                // every peer's C (peer access enabled by ensure_peer)
+                void* peers[vk::kMaxPeers];
+                int np = 0;
+                for (int peer = 0; peer < n_gpu; ++peer)
+                    if (peer != r)
+                        peers[np++] = static_cast<char*>(a->C[peer]) + static_cast<size_t>(off[r] + c0) * a->n * esize;
+                rc = ga.m > 0 ? vk_gemm_peers(&ga, peers, np) : VK_OK;
+            } else {
+                rc = vk_gemm(&ga);
+            }
             if (rc != VK_OK || !pipelined) break;
             e = cudaEventRecord(g->ev_chunk[r][q], g->streams[r]);
             if (e == cudaSuccess) e = cudaStreamWaitEvent(g->copy_streams[r], g->ev_chunk[r][q], 0);
@@ -278,6 +295,10 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
                 cudaEventDestroy(copies_done);
             }
         }
+        if (fused) {  // C is complete on GPU r once every GPU's kernel (and so its peer stores) finished
+            for (int q = 0; q < n_gpu; ++q)
+                if (q != r) cudaStreamWaitEvent(g->streams[r], g->ev_compute[q], 0);
+        }
         cudaEventRecord(g->ev_gather[r], g->streams[r]);
         e = cudaStreamSynchronize(g->streams[r]);
         if (e != cudaSuccess && rc == VK_OK) rc = cuda_err(e, "shard synchronize");
@@ -292,7 +313,7 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
     cudaSetDevice(prev);
     if (rc == VK_OK && a->times_ms != nullptr) {
         a->times_ms[0] = t_compute;
-        a->times_ms[1] = (gather || pipelined) ? t_gather : 0.f;
+        a->times_ms[1] = (gather || pipelined || fused) ? t_gather : 0.f;
     }
     return rc;
 }

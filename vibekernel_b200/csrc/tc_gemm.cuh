@@ -45,6 +45,7 @@
 #include <type_traits>
 
 #include "ptx.cuh"
+#include "vk_internal.h"
 
 namespace vk {
 
@@ -57,6 +58,10 @@ struct TcParams {
     float* C32;              // optional fp32 copy, ld = N
     int vec_ok;              // C / C32 alignment allows 16-byte stores
     int c_tma;               // 1: fp16 C is written by TMA tile stores through the C tensor map
+    // fused all-gather: every finished 32 x 32 box of fp16 C is also stored (plain 16-byte stores over
+    // NVLink, never TMA) at the same row / column offsets into each peer GPU's C buffer (same ldc)
+    int npeers;
+    __half* peer_c[kMaxPeers];
     unsigned long long timeout_ns;
     // work units: full_units whole tiles and the tail tiles, each cut either into two column
     // halves (nsplit = 1: BN/2-wide MMAs, no reduction) or into `split` k-slices; the whole tiles
@@ -200,6 +205,38 @@ __device__ __forceinline__ void tmem_words_to_f32(const uint32_t (&r)[32], float
     }
 }
 
+// Fused all-gather: one warp copies its staged 32 x 32 fp16 box (rows row0.., columns col..; row r's
+// 64 bytes at `pitch`, 16-byte chunk j at j ^ ((r >> 1) & 3) when `swizzled`) into every peer's C,
+// 4 lanes per row so each store instruction writes 64-byte runs of 8 rows.  Same bounds as the local
+// stores (row < M, column < N); 16-byte stores only when the row segment is whole and aligned.
+__device__ __forceinline__ void store_box_to_peers(const TcParams& p, const uint8_t* box, int pitch, bool swizzled,
+                                                   int row0, int lane, int col)
+{
+    const int seg = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int rr = (lane >> 2) + 8 * j;
+        const int grow = row0 + rr;
+        const int gcol = col + seg * 8;
+        if (grow >= p.M || gcol >= p.N) continue;
+        const int chunk = swizzled ? (seg ^ ((rr >> 1) & 3)) : seg;
+        const uint4 v = *reinterpret_cast<const uint4*>(box + rr * pitch + chunk * 16);
+        const long long off = static_cast<long long>(grow) * p.ldc + gcol;
+        const bool whole = gcol + 8 <= p.N && p.vec_ok;
+#pragma unroll 1
+        for (int q = 0; q < p.npeers; ++q) {
+            __half* dst = p.peer_c[q] + off;
+            if (whole) {
+                *reinterpret_cast<uint4*>(dst) = v;
+            } else {
+                const __half* h = reinterpret_cast<const __half*>(&v);
+                for (int e = 0; e < 8; ++e)
+                    if (gcol + e < p.N) dst[e] = h[e];
+            }
+        }
+    }
+}
+
 // One warp writes its 32 rows x 32 columns of C (this lane's row = row0 + lane, values f for
 // columns col .. col+31): the fused epilogue and the fp32 copy are applied per row, then the fp16
 // results go through the warp's staging buffer.  With a C tensor map (c_tma) lane 0 stores the
@@ -207,6 +244,9 @@ __device__ __forceinline__ void tmem_words_to_f32(const uint32_t (&r)[32], float
 // alternate, and a buffer is rewritten only after the store issued from it two chunks earlier has
 // read it.  Otherwise each global store instruction writes 64-byte runs of 8 rows (4 lanes per row)
 // instead of 16 bytes of 32 different rows.
+// PEERS: compiled only into the kernel instance that serves vk_gemm_peers, so the default kernels'
+// epilogue code stays exactly as it is without peer stores.
+template <bool PEERS>
 __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap* tmap_c, uint8_t* stg, int row0,
                                            int lane, int col, float (&f)[32], uint32_t& nbuf)
 {
@@ -253,6 +293,7 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
             tma_store_2d(tmap_c, smem_u32(buf), col, row0);
             bulk_commit_group();
         }
+        if constexpr (PEERS) store_box_to_peers(p, buf, 64, true, row0, lane, col);
         ++nbuf;
         return;
     }
@@ -262,6 +303,7 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
         srow[j] = make_uint4(pack_half2(f[8 * j], f[8 * j + 1]), pack_half2(f[8 * j + 2], f[8 * j + 3]),
                              pack_half2(f[8 * j + 4], f[8 * j + 5]), pack_half2(f[8 * j + 6], f[8 * j + 7]));
     __syncwarp();
+    if constexpr (PEERS) store_box_to_peers(p, stg, kEpiPitch, false, row0, lane, col);
     const int seg = lane & 3;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -284,7 +326,7 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
     __syncwarp();
 }
 
-template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32, bool PEERS = false>
 __global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_c, const TcParams p)
@@ -631,7 +673,7 @@ __global__ void __launch_bounds__(192, 1)
                                     }
                                 }
                             }
-                            store_rows(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                            store_rows<PEERS>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                         }
                     } else if (ok) {
                         __threadfence();
@@ -700,7 +742,7 @@ __global__ void __launch_bounds__(192, 1)
                                         }
                                     }
                                 }
-                                store_rows(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                                store_rows<PEERS>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                             }
                             __syncwarp();
                         }
@@ -719,7 +761,7 @@ __global__ void __launch_bounds__(192, 1)
                     if (col0 + c < p.N) {
                         float f[32];
                         tmem_words_to_f32<ACC_F32>(r, f);
-                        store_rows(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                        store_rows<PEERS>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                     }
                 }
             }

@@ -2,6 +2,9 @@
 #pragma once
 
 namespace vk {
+// Most peer C buffers one launch of the fused all-gather (vk_gemm_peers) stores into: an 8-GPU node.
+constexpr int kMaxPeers = 7;
+
 // Records a thread-local error message (read back by vk_last_error_string) and returns `code`.
 int set_error(int code, const char* fmt, ...);
 // Frees per-device scratch owned by the library (vk_shutdown).

@@ -451,13 +451,16 @@ struct Problem {
     const void* Cin = nullptr;
     int64_t ldcin = 0;
     const void* bias = nullptr;
+    // vk_gemm_peers: peer C buffers that also receive every finished box of C (tensor-core path only)
+    int npeers = 0;
+    void* peer_c[kMaxPeers] = {};
 };
 
-template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32, bool PEERS = false>
 static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScratch* fixed)
 {
     using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32>;
-    auto fn = tc_gemm_kernel<CG, BN, STAGES, KA, ACC_F32>;
+    auto fn = tc_gemm_kernel<CG, BN, STAGES, KA, ACC_F32, PEERS>;
     int max_units = 0;
     int rc = kernel_slot(st, fn, Cfg::kSmemBytes, Cfg::kThreads, CG, &max_units);
     if (rc != VK_OK) return rc;
@@ -485,7 +488,13 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     p.C32 = pb.C32;
     const bool c_vec = (reinterpret_cast<uintptr_t>(pb.C) % 16 == 0) && (pb.ldc % 8 == 0);
     const bool c32_vec = pb.C32 == nullptr || ((reinterpret_cast<uintptr_t>(pb.C32) % 16 == 0) && (pb.n % 4 == 0));
-    p.vec_ok = (c_vec && c32_vec) ? 1 : 0;
+    bool peers_vec = true;
+    p.npeers = pb.npeers;
+    for (int q = 0; q < kMaxPeers; ++q) {
+        p.peer_c[q] = q < pb.npeers ? static_cast<__half*>(pb.peer_c[q]) : nullptr;
+        if (q < pb.npeers) peers_vec = peers_vec && reinterpret_cast<uintptr_t>(pb.peer_c[q]) % 16 == 0;
+    }
+    p.vec_ok = (c_vec && c32_vec && peers_vec) ? 1 : 0;
     // TMA stores of C need a 16-byte aligned base and a pitch that is a multiple of 16 bytes
     CUtensorMap tc;
     memset(&tc, 0, sizeof(tc));
@@ -562,6 +571,14 @@ template <bool F32>
 static int launch_tc_variant(DeviceState& st, int dev, const Problem& pb, int algo, const FixedScratch* fixed)
 {
     const int tn = pb.tile_n ? pb.tile_n : 256;
+    if (pb.npeers > 0) {
+        // the peer-storing epilogue is compiled into the default pair kernel only
+        if (algo == VK_ALGO_TC_2SM && tn == 256 && g_bk_2sm256.load(std::memory_order_relaxed) == 128)
+            return launch_tc<2, 256, 3, 2, F32, true>(st, dev, pb, fixed);
+        return set_error(VK_ERR_UNSUPPORTED,
+                         "vk_gemm_peers: peer stores run on the default pair kernel only (algo AUTO or TC_2SM, "
+                         "tile_n 256, bk_2sm256 128)");
+    }
     if (algo == VK_ALGO_TC_2SM) {
         if (tn == 256) {
             if (g_bk_2sm256.load(std::memory_order_relaxed) == 128) return launch_tc<2, 256, 3, 2, F32>(st, dev, pb, fixed);
@@ -714,7 +731,8 @@ void release_device_state()
 // ==========================================================================================
 using namespace vk;
 
-static int gemm_entry(const vk_gemm_args* a, const vk_gemm_ext* x, const char* name)
+static int gemm_entry(const vk_gemm_args* a, const vk_gemm_ext* x, const char* name, void* const* peers = nullptr,
+                      int npeers = 0)
 {
     if (a == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "%s: args is NULL", name);
     if (a->m < 0 || a->n < 0 || a->k < 0)
@@ -778,6 +796,19 @@ static int gemm_entry(const vk_gemm_args* a, const vk_gemm_ext* x, const char* n
     if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256)
         return set_error(VK_ERR_INVALID_ARGUMENT, "%s: tile_n must be 0, 128 or 256", name);
 
+    if (npeers < 0 || npeers > kMaxPeers)
+        return set_error(VK_ERR_INVALID_ARGUMENT, "%s: npeers must be 0..%d", name, kMaxPeers);
+    if (npeers > 0) {
+        if (peers == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "%s: peer_C is NULL", name);
+        for (int q = 0; q < npeers; ++q) {
+            if (peers[q] == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "%s: peer_C[%d] is NULL", name, q);
+            pb.peer_c[q] = peers[q];
+        }
+        if (a->dtype != VK_DTYPE_F16)
+            return set_error(VK_ERR_UNSUPPORTED, "%s: peer stores are for the fp16 tensor-core kernels", name);
+        pb.npeers = npeers;
+    }
+
     int dev = 0;
     DeviceState* st = nullptr;
     int rc = current_device(&dev, &st);
@@ -789,12 +820,19 @@ extern "C" int vk_gemm(const vk_gemm_args* a) { return gemm_entry(a, nullptr, "v
 
 extern "C" int vk_gemm_ex(const vk_gemm_args* a, const vk_gemm_ext* x) { return gemm_entry(a, x, "vk_gemm_ex"); }
 
+extern "C" int vk_gemm_peers(const vk_gemm_args* a, void* const* peer_C, int32_t npeers)
+{
+    return gemm_entry(a, nullptr, "vk_gemm_peers", peer_C, npeers);
+}
+
 namespace vk {
 int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc, int algo_in)
 {
     DeviceState* st = &st_ref;
     if (pb.m == 0 || pb.n == 0) return VK_OK;
     if (pb.C == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: C is NULL");
+    if (pb.npeers > 0 && (pb.k == 0 || algo_in == VK_ALGO_SIMT || algo_in == VK_ALGO_FFMA))
+        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm_peers: peer stores need the tensor-core kernels and k > 0");
     if (pb.k == 0) return dtype == VK_DTYPE_F16 ? launch_zero<__half>(*st, pb) : launch_zero<float>(*st, pb);
     if (pb.A == nullptr || pb.B == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: A or B is NULL");
 
@@ -841,6 +879,10 @@ int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc
                                  : launch_tc_variant<false>(*st, dev, pk, VK_ALGO_TC_2SM, nullptr);
     }
     if (algo == VK_ALGO_AUTO) algo = tma_ok ? VK_ALGO_TC_2SM : VK_ALGO_SIMT;
+    if (algo == VK_ALGO_SIMT && pb.npeers > 0)
+        return set_error(VK_ERR_UNSUPPORTED,
+                         "vk_gemm_peers: these operands need the predicated kernel (enable \"repack\"), which has no "
+                         "peer stores");
     if (algo == VK_ALGO_SIMT) {
         if (acc != VK_ACC_F32)
             return set_error(VK_ERR_UNSUPPORTED, "vk_gemm: the predicated CUDA-core kernel accumulates in fp32 only");

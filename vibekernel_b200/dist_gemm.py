@@ -6,10 +6,11 @@ all-gather of the C row blocks, in place in a full [m, n] buffer on every rank: 
 so each rank's block is one contiguous span.  Two ways:
   * ``allgather_rows``: NCCL (over NVLink on B200; gloo in the CPU tests) after the GEMM;
   * ``PeerRowGather``: overlapped with the GEMM.  Every rank maps the peers' C buffers into its
-    process once (CUDA IPC), computes its rows in chunks and, as each chunk finishes, pushes it
-    into every peer's C with the copy engines (no SMs taken from the GEMM) while the next chunk
-    is computed; a one-element all-reduce at the end completes on every rank only after every
-    rank's pushes have.
+    process once (CUDA IPC).  Mode "pipelined": it computes its rows in chunks and, as each chunk
+    finishes, pushes it into every peer's C with the copy engines (no SMs taken from the GEMM)
+    while the next chunk is computed.  Mode "fused": one GEMM whose epilogue stores every finished
+    box of C into the peers' C as well (vk_gemm_peers, plain stores over NVLink).  Either way a
+    one-element all-reduce at the end completes on every rank only after every rank's stores have.
 The reference has no multi-GPU path (README.md:161); this is the layer BASELINE.json asks for.
 """
 from __future__ import annotations
@@ -74,10 +75,11 @@ class PeerRowGather:
         self.streams = {p: torch.cuda.Stream(device=dev) for p in self.peers}  # one copy queue per peer
         self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
 
-    def run(self, A_local, B, gemm, chunks: int = 2):
-        """``gemm(A_rows, B, C_rows)`` on each chunk of this rank's rows; each finished chunk is
-        pushed to every peer while the next one is computed.  Returns when (stream order) every
-        rank's C_full is complete."""
+    def run(self, A_local, B, gemm, chunks: int = 2, mode: str = "pipelined"):
+        """Mode "pipelined": ``gemm(A_rows, B, C_rows)`` on each chunk of this rank's rows, each
+        finished chunk pushed to every peer while the next one is computed.  Mode "fused": one
+        ``gemm(A_local, B, C_rows, peers=[...])`` whose epilogue stores into the peers' C itself.
+        Returns when (stream order) every rank's C_full is complete."""
         import torch
         import torch.distributed as dist
         from . import copy_async
@@ -85,6 +87,14 @@ class PeerRowGather:
         row_bytes = C.stride(0) * C.element_size()
         base = C.data_ptr()
         compute = torch.cuda.current_stream(C.device)
+        if mode == "fused":
+            lo, hi = self.off[self.rank], self.off[self.rank + 1]
+            if hi > lo:
+                gemm(A_local, B, C[lo:hi], peers=[self.peers[p] + lo * row_bytes for p in sorted(self.peers)])
+            dist.all_reduce(self.flag, group=self.group)
+            return C
+        if mode != "pipelined":
+            raise ValueError(f"unknown mode {mode!r}")
         for (r0, r1), copies in push_plan(self.off, self.rank, chunks, row_bytes):
             lo = self.off[self.rank]
             gemm(A_local[r0:r1], B, C[lo + r0:lo + r1])
