@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this folder from the reference's own v0 ground truth.
 
-Run in a container that holds the reference tree (it builds ``oracle/_ref`` from the
-reference's unmodified v0 sources first):
+Run where the reference tree is available (it builds ``oracle/_ref`` from the reference's
+unmodified v0 sources first):
 
     make -C oracle && python tests/golden/make_golden.py
 
