@@ -229,6 +229,8 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *   "tma_store"       1 (default) = the tensor-core kernels write fp16 C with TMA tile stores when C
  *                     is 16-byte aligned with a pitch that is a multiple of 8 elements; 0 = always
  *                     per-lane coalesced stores (the path taken for any other C)
+ *   "l2_evict_last"   1 (default) = the tensor-core kernels load A and B tiles with an L2
+ *                     evict_last cache policy; 0 = default caching
  *   "raster_group"    tiles along M per rasterisation group of the persistent scheduler (8)
  *   "bk_2sm256"       k per pipeline stage of the 256-column pair kernel: 128 (default, 3 stages
  *                     of 64 KB) or 64 (6 stages of 32 KB)

@@ -384,11 +384,13 @@ def test_tail_split_matches_unsplit(vk, shape):
         assert v0.max_elem_rel(c, g32) <= ELEM
 
 
-PIPELINE_OPTIONS = [{"bk_2sm256": 64}, {"bk_2sm256": 64, "tail_split": 0}, {"tail_split": 0}, {"tma_store": 0}]
-_DEFAULTS = {"bk_2sm256": 128, "tail_split": 1, "tma_store": 1}
+PIPELINE_OPTIONS = [{"bk_2sm256": 64}, {"bk_2sm256": 64, "tail_split": 0}, {"tail_split": 0}, {"tma_store": 0},
+                    {"l2_evict_last": 0}]
+_DEFAULTS = {"bk_2sm256": 128, "tail_split": 1, "tma_store": 1, "l2_evict_last": 1}
 
 
-@pytest.mark.parametrize("opts", PIPELINE_OPTIONS, ids=["bk64", "bk64-nosplit", "bk128-nosplit", "lane-stores"])
+@pytest.mark.parametrize("opts", PIPELINE_OPTIONS, ids=["bk64", "bk64-nosplit", "bk128-nosplit", "lane-stores",
+                                                        "no-l2-hint"])
 @pytest.mark.parametrize("shape", [(1024, 1024, 1024), (4096, 4096, 4096), (4000, 5120, 3000), (200, 136, 72),
                                    (256, 256, 4096)])
 @pytest.mark.parametrize("acc", ["f32", "f16"])

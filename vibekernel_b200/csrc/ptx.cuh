@@ -187,6 +187,35 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* map, 
         : "memory");
 }
 
+// L2 cache policy that keeps the lines a load brings in resident over others (evict_last).
+__device__ __forceinline__ uint64_t l2_policy_evict_last()
+{
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// tma_load_2d / tma_load_2d_pair with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const void* map, uint32_t bar, int32_t c0, int32_t c1,
+                                                 uint64_t pol)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const void* map, uint32_t bar_cluster, int32_t c0,
+                                                      int32_t c1, uint64_t pol)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "l"(pol)
+        : "memory");
+}
+
 // Contiguous bulk copy global -> this CTA's shared memory (no tensor map); both addresses 16-byte
 // aligned, size a multiple of 16.  Completion bytes go to `bar` in this CTA.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)

@@ -60,6 +60,7 @@ struct TcParams {
     int c_tma;               // 1: fp16 C is written by TMA tile stores through the C tensor map
     // fused all-gather: every finished 32 x 32 box of fp16 C is also stored (plain 16-byte stores over
     // NVLink, never TMA) at the same row / column offsets into each peer GPU's C buffer (same ldc)
+    int l2_evict_last;       // 1: operand tiles are loaded with an L2 evict_last policy
     int npeers;
     __half* peer_c[kMaxPeers];
     unsigned long long timeout_ns;
@@ -406,6 +407,7 @@ __global__ void __launch_bounds__(192, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            const uint64_t l2_pol = p.l2_evict_last ? l2_policy_evict_last() : 0ull;
             trace_at(p.trace, 2);
             for (int u = cluster_id; ok && u < p.units; u += num_clusters) {
                 const Unit w = unit_info(p, u);
@@ -433,10 +435,17 @@ __global__ void __launch_bounds__(192, 1)
                         bar = mapa_shared(fb, 0);
                     }
                     auto load = [&](uint32_t dst, const CUtensorMap* map, int c0, int c1) {
-                        if constexpr (CG == 1)
-                            tma_load_2d(dst, map, bar, c0, c1);
-                        else
-                            tma_load_2d_pair(dst, map, bar, c0, c1);
+                        if (p.l2_evict_last) {
+                            if constexpr (CG == 1)
+                                tma_load_2d_hint(dst, map, bar, c0, c1, l2_pol);
+                            else
+                                tma_load_2d_pair_hint(dst, map, bar, c0, c1, l2_pol);
+                        } else {
+                            if constexpr (CG == 1)
+                                tma_load_2d(dst, map, bar, c0, c1);
+                            else
+                                tma_load_2d_pair(dst, map, bar, c0, c1);
+                        }
                     };
                     if (!p.a_mn) {
 #pragma unroll

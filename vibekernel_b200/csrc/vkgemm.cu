@@ -135,6 +135,9 @@ static std::atomic<int> g_tail_split{1};
 static std::atomic<int> g_tail_nsplit{1};
 static std::atomic<int> g_tail_first{1};
 static std::atomic<int> g_tma_store{1};
+// Operand tiles are loaded with an L2 evict_last policy: they stay resident over the C stores,
+// the k-slice partials and whatever the previous kernel left dirty in L2 (+0.4 to +1 % measured).
+static std::atomic<int> g_l2_evict_last{1};
 static std::atomic<int> g_raster_group{8};
 // k depth per pipeline stage of the 256-column pair kernel.  Every stage ends with tcgen05.commit
 // to both CTAs' "empty" barriers, and those commits measurably throttle the tensor pipe; 128-deep
@@ -489,6 +492,7 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
     const bool c_vec = (reinterpret_cast<uintptr_t>(pb.C) % 16 == 0) && (pb.ldc % 8 == 0);
     const bool c32_vec = pb.C32 == nullptr || ((reinterpret_cast<uintptr_t>(pb.C32) % 16 == 0) && (pb.n % 4 == 0));
     bool peers_vec = true;
+    p.l2_evict_last = g_l2_evict_last.load(std::memory_order_relaxed);
     p.npeers = pb.npeers;
     for (int q = 0; q < kMaxPeers; ++q) {
         p.peer_c[q] = q < pb.npeers ? static_cast<__half*>(pb.peer_c[q]) : nullptr;
@@ -1095,6 +1099,10 @@ extern "C" int vk_set_option(const char* name, int64_t value)
     }
     if (strcmp(name, "tail_first") == 0) {
         g_tail_first.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
+    if (strcmp(name, "l2_evict_last") == 0) {
+        g_l2_evict_last.store(value != 0 ? 1 : 0);
         return VK_OK;
     }
     if (strcmp(name, "tma_store") == 0) {
