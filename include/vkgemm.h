@@ -200,7 +200,10 @@ int vk_copy_async(void* dst, const void* src, size_t bytes, void* stream);
 
 /* Device and library state. */
 int vk_init(int device);                 /* optional: warm per-device state (SM count, attrs) */
-int vk_shutdown(void);                   /* frees per-device state and NCCL communicators    */
+int vk_shutdown(void);                   /* frees per-device state and NCCL communicators;
+                                            call it before any cudaDeviceReset, since the library
+                                            caches per-context facts (kernel attributes, the
+                                            no-allocation array's address) until then            */
 const char* vk_last_error_string(void);  /* thread-local message for the last failure        */
 const char* vk_version_string(void);
 

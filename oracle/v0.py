@@ -122,11 +122,38 @@ def ref_available() -> bool:
     return os.path.exists(REF_LIB_PATH)
 
 
+# OpenBLAS picks its sgemm kernel by CPU model at load time, and kernels sum in different orders,
+# so the same reference v0 gives fp16 outputs that differ by one ulp on ~0.2 % of elements between
+# CPU generations.  The golden fixtures were produced with OpenBLAS's "Cooperlake" kernel (AVX-512
+# with BF16); on any CPU that can run it, that kernel is pinned before the library loads, so the
+# reference reproduces the fixtures bit for bit whatever the host.  Elsewhere the automatic choice
+# stays and the fixture tests compare within one ulp instead.
+PINNED_CORETYPE = "Cooperlake"
+
+
+def _cpu_flags() -> set:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    return set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    return set()
+
+
+def coretype_pinned() -> bool:
+    """True when the reference library runs (or will run) the fixtures' OpenBLAS kernel."""
+    return os.environ.get("OPENBLAS_CORETYPE") == PINNED_CORETYPE
+
+
 def _ref():
     global _ref_lib
     if _ref_lib is None:
         if not ref_available():
             raise RuntimeError(f"{REF_LIB_PATH} is not built (make -C oracle)")
+        if "OPENBLAS_CORETYPE" not in os.environ and {"avx512f", "avx512_bf16"} <= _cpu_flags():
+            os.environ["OPENBLAS_CORETYPE"] = PINNED_CORETYPE
         lib = ctypes.CDLL(REF_LIB_PATH)
         sz = ctypes.c_size_t
         vp = ctypes.c_void_p

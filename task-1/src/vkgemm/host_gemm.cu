@@ -14,7 +14,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/vkgemm.h"
+#include "vkgemm.h"
 #include "vk_internal.h"
 
 namespace {

@@ -13,7 +13,7 @@
 #include <mutex>
 #include <vector>
 
-#include "../../include/vkgemm.h"
+#include "vkgemm.h"
 #include "vk_internal.h"
 
 namespace {

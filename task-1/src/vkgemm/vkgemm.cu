@@ -16,7 +16,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/vkgemm.h"
+#include "vkgemm.h"
 #include "ptx.cuh"
 #include "simt_gemm.cuh"
 #include "tc_gemm.cuh"
@@ -147,6 +147,8 @@ static std::atomic<int> g_sgemm_v2{1};
 static std::atomic<int> g_sgemm_paired{1};
 static std::atomic<int> g_repack{1};
 static std::atomic<int> g_clock_probe_on{0};
+// Devices (bit per ordinal < 31) on which each SGEMM variant's shared-memory attribute is set.
+static std::atomic<int> g_sgemm_attr_mask[3] = {{0}, {0}, {0}};
 static std::atomic<int> g_trace_on{0};
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -624,7 +626,7 @@ static int launch_sgemm(const Problem& pb)
         // 2 = paired FMAs, 8 x 8 per thread (49.8); 0 = scalar FMAs, 8 x 8 (42.2).  A variant that stored
         // the A tile pre-broadcast as (a, a) pairs (register-staged A) measured 10 % slower than the
         // register broadcast and was dropped.
-        static std::atomic<int> attr_dev_mask[3] = {{0}, {0}, {0}};
+        std::atomic<int>* attr_dev_mask = g_sgemm_attr_mask;
         const int variant = g_sgemm_paired.load(std::memory_order_relaxed);
         auto fn = variant == 1 ? sgemm_ffma_w16_kernel
                                : (variant == 2 ? sgemm_ffma_v2_kernel<true> : sgemm_ffma_v2_kernel<false>);
@@ -706,6 +708,7 @@ void release_device_state()
     std::lock_guard<std::mutex> lk(g_mu);
     int prev = 0;
     cudaGetDevice(&prev);
+    for (std::atomic<int>& m : g_sgemm_attr_mask) m.store(0);
     for (int d = 0; d < kMaxDevices; ++d) {
         DeviceState& st = g_dev[d];
         {
@@ -713,6 +716,12 @@ void release_device_state()
             for (TmapEntry& e : st.tmaps) e = TmapEntry();
             st.tmap_next = 0;
         }
+        // Per-context facts cached on first use: the device address of the no-allocation array and
+        // the kernels' shared-memory attributes.  A later cudaDeviceReset would make them stale, so
+        // they are looked up again after vk_shutdown.
+        st.noalloc_scratch.store(nullptr, std::memory_order_release);
+        st.num_kernels.store(0, std::memory_order_release);
+        for (KernelSlot& k : st.kernels) k = KernelSlot();
         if (st.num_scratch == 0) continue;
         cudaSetDevice(d);
         for (int i = 0; i < st.num_scratch; ++i) {

@@ -48,7 +48,7 @@ def test_cli_help_and_errors(built):
 
 def _scan_files():
     out = []
-    for base in ("task-1/src", "task-1/include", "vibekernel_b200/csrc", "include"):
+    for base in ("task-1/src", "task-1/include", "include"):
         for dp, _, fs in os.walk(os.path.join(ROOT, base)):
             for f in fs:
                 if f.endswith((".cu", ".cuh", ".cpp", ".hpp", ".h")) and not re.search(r"_v0(_|\.)", f):

@@ -70,7 +70,13 @@ def test_reference_build_reproduces_fixture(path):
     rows = z["rows"]
     if str(z["dtype"]) == "f16":
         out = v0.ref_v0_f16(A[rows], B)
-        assert np.array_equal(out.view(np.uint16), z["C"].view(np.uint16))
+        if v0.coretype_pinned():
+            # the fixtures' OpenBLAS kernel: bit for bit
+            assert np.array_equal(out.view(np.uint16), z["C"].view(np.uint16))
+        else:
+            # another OpenBLAS kernel sums in another order: one fp16 ulp on a few elements
+            assert np.mean(out.view(np.uint16) != z["C"].view(np.uint16)) < 0.01
+            assert v0.max_elem_rel(out, z["C"]) < 2e-3
     else:
         out = v0.ref_v0_f32(A[rows], B)
         assert np.allclose(out, z["C"], rtol=0, atol=1e-4)
