@@ -114,6 +114,38 @@ int vk_gemm_ex(const vk_gemm_args* args, const vk_gemm_ext* ext);
  * or a collective).  fp16 only; operands that would need the predicated kernel are rejected. */
 int vk_gemm_peers(const vk_gemm_args* args, void* const* peer_C, int32_t npeers);
 
+/* Fused compute + all-gather through NVLink SHARP multicast (no counterpart in the reference): vk_gemm
+ * for the fp16 tensor-core kernels whose epilogue stores every finished box of C ONCE, with
+ * multimem.st, to C_mc -- the multicast view of the same bytes as C in a buffer from vk_mc_alloc
+ * (one process) or vk_mc_attach (one process per GPU).  The NVSwitch writes each box into the same
+ * offset of every member GPU's buffer, this GPU's included, so C is not stored locally as well and the
+ * SMs issue 1/(P-1) of the bytes of vk_gemm_peers.  C must lie inside the calling device's view of a
+ * live multicast buffer and C_mc must be its multicast address (checked); n and ldc multiples of 8.
+ * The caller orders the other GPUs' reads after this kernel (an event join or a collective). */
+int vk_gemm_mc(const vk_gemm_args* args, void* C_mc);
+
+/* Multicast (NVLS) buffers, no counterpart in the reference.  A buffer has one view per member GPU
+ * (that GPU's own memory, used as its full C) and one multicast view.  Needs an NVSwitch system
+ * (vk_mc_supported).  Teardown rule: every member must have finished with the buffer (synchronise and
+ * barrier) before any member frees / detaches it, and no member may exit while attached.
+ *   vk_mc_supported  *out = 1 when `device` supports NVLS multicast.
+ *   vk_mc_alloc      one process, ndev GPUs: ptrs[i] = device i's view (bytes, rounded up to the
+ *                    multicast granularity), *mc_ptr = the multicast view; vk_mc_free(mc_ptr) frees.
+ *   vk_mc_create     one process per GPU, on the owner: creates the object for `members` GPUs and
+ *                    exports it; share[3] = {owner pid, descriptor, padded bytes} to send to the others.
+ *   vk_mc_import     on every other member: fetches the owner's descriptor (pidfd_getfd, same node).
+ *   vk_mc_attach     on every member (owner included), collectively: adds the device, creates and binds
+ *                    its memory (blocks until every member has attached) and maps both views.
+ *   vk_mc_detach     on every member, after a barrier: unmaps, unbinds and releases this member. */
+typedef struct vk_mc_team vk_mc_team;
+int vk_mc_supported(int device, int* out);
+int vk_mc_alloc(int32_t ndev, const int32_t* devices, size_t bytes, void** ptrs, void** mc_ptr);
+int vk_mc_free(void* mc_ptr);
+int vk_mc_create(int device, int32_t members, size_t bytes, vk_mc_team** team, int64_t* share);
+int vk_mc_import(int device, int32_t members, const int64_t* share, vk_mc_team** team);
+int vk_mc_attach(vk_mc_team* team, void** local_ptr, void** mc_ptr, size_t* bytes);
+int vk_mc_detach(vk_mc_team* team);
+
 /* No counterpart in the reference.  Same contract as vk_gemm for the fp16 tensor-core kernels
  * (algo AUTO, TC_2SM or TC_1SM; 16-byte aligned A/B with lda, ldb multiples of 8), for callers
  * that cannot allocate device memory: code running during CUDA graph capture, applications whose
@@ -172,7 +204,10 @@ typedef struct vk_shard_args {
                                  every finished chunk to all peers with peer-to-peer copies (copy
                                  engines over NVLink) while the next chunk is computed;
                                  3 = fused: each GPU's epilogue stores every finished box of C into
-                                 all peers' C as well (vk_gemm_peers; fp16, at most 8 GPUs) */
+                                 all peers' C as well (vk_gemm_peers; fp16, at most 8 GPUs);
+                                 4 = NVLS: C[r] are the views of one vk_mc_alloc buffer and each
+                                 GPU's epilogue stores every box once to its multicast view
+                                 (vk_gemm_mc; fp16) */
     float* times_ms;          /* optional, length 2: [0] compute max over GPUs, [1] all-gather */
 } vk_shard_args;
 

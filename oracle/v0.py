@@ -142,8 +142,15 @@ def _cpu_flags() -> set:
     return set()
 
 
+def _pin_coretype() -> None:
+    if "OPENBLAS_CORETYPE" not in os.environ and {"avx512f", "avx512_bf16"} <= _cpu_flags():
+        os.environ["OPENBLAS_CORETYPE"] = PINNED_CORETYPE
+
+
 def coretype_pinned() -> bool:
     """True when the reference library runs (or will run) the fixtures' OpenBLAS kernel."""
+    if _ref_lib is None:
+        _pin_coretype()
     return os.environ.get("OPENBLAS_CORETYPE") == PINNED_CORETYPE
 
 
@@ -152,8 +159,7 @@ def _ref():
     if _ref_lib is None:
         if not ref_available():
             raise RuntimeError(f"{REF_LIB_PATH} is not built (make -C oracle)")
-        if "OPENBLAS_CORETYPE" not in os.environ and {"avx512f", "avx512_bf16"} <= _cpu_flags():
-            os.environ["OPENBLAS_CORETYPE"] = PINNED_CORETYPE
+        _pin_coretype()
         lib = ctypes.CDLL(REF_LIB_PATH)
         sz = ctypes.c_size_t
         vp = ctypes.c_void_p
@@ -185,3 +191,19 @@ def ref_v0_f32(A: np.ndarray, B: np.ndarray) -> np.ndarray:
     C = np.zeros((m, n), dtype=np.float32)
     _ref().vk_ref_v0_f32(m, n, k, A.ctypes.data, B.ctypes.data, C.ctypes.data)
     return C
+
+
+def set_ref_threads(n: int) -> None:
+    """Thread count of the OpenBLAS under the reference v0 (openblas_set_num_threads)."""
+    lib = _ref()
+    fn = lib.openblas_set_num_threads  # resolved through the library's dependency (OpenBLAS)
+    fn.argtypes = [ctypes.c_int]
+    fn.restype = None
+    fn(int(n))
+
+
+def ref_threads() -> int:
+    fn = _ref().openblas_get_num_threads
+    fn.argtypes = []
+    fn.restype = ctypes.c_int
+    return int(fn())

@@ -176,13 +176,18 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
         cudaSetDevice(prev);
         return rc;
     }
-    if (a->allgather_c < 0 || a->allgather_c > 3) {
+    if (a->allgather_c < 0 || a->allgather_c > 4) {
         cudaSetDevice(prev);
-        return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: allgather_c must be 0, 1, 2 or 3");
+        return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_sharded: allgather_c must be 0..4");
     }
     const bool pipelined = a->allgather_c == 2 && n_gpu > 1;
     const bool gather = a->allgather_c == 1 && n_gpu > 1;
     const bool fused = a->allgather_c == 3 && n_gpu > 1;
+    const bool nvls = a->allgather_c == 4 && n_gpu > 1;
+    if (nvls && a->dtype != VK_DTYPE_F16) {
+        cudaSetDevice(prev);
+        return vk::set_error(VK_ERR_UNSUPPORTED, "vk_gemm_sharded: the NVLS gather takes fp16");
+    }
     if (fused && (n_gpu - 1 > vk::kMaxPeers || a->dtype != VK_DTYPE_F16)) {
         cudaSetDevice(prev);
         return vk::set_error(VK_ERR_UNSUPPORTED, "vk_gemm_sharded: the fused gather takes fp16 and at most %d GPUs",
@@ -232,7 +237,19 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
             ga.acc = a->acc;
             ga.algo = a->algo;
             ga.stream = g->streams[r];
-            if (fused) {
+            if (nvls) {
+                // NVLS gather: C[r] is GPU r's view of one multicast buffer (vk_mc_alloc); the epilogue
+                // stores every finished box once to the multicast view of its rows and the switch
+                // writes it into every GPU's C
+                void* mc = vk::mc_lookup(a->devices[r], a->C[r], static_cast<size_t>(a->m) * a->n * esize);
+                if (mc == nullptr) {
+                    rc = vk::set_error(VK_ERR_INVALID_ARGUMENT,
+                                       "vk_gemm_sharded: allgather_c 4 needs C[%d] from vk_mc_alloc", r);
+                    break;
+                }
+                rc = ga.m > 0 ? vk_gemm_mc(&ga, static_cast<char*>(mc) + static_cast<size_t>(off[r] + c0) * a->n * esize)
+                              : VK_OK;
+            } else if (fused) {
                 // fused gather: the epilogue also stores every finished box into the same rows of
                 // every peer's C (peer access enabled by ensure_peer)
                 void* peers[vk::kMaxPeers];
@@ -295,7 +312,7 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
                 cudaEventDestroy(copies_done);
             }
         }
-        if (fused) {  // C is complete on GPU r once every GPU's kernel (and so its peer stores) finished
+        if (fused || nvls) {  // C is complete on GPU r once every GPU's kernel (and its stores) finished
             for (int q = 0; q < n_gpu; ++q)
                 if (q != r) cudaStreamWaitEvent(g->streams[r], g->ev_compute[q], 0);
         }
@@ -313,7 +330,7 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
     cudaSetDevice(prev);
     if (rc == VK_OK && a->times_ms != nullptr) {
         a->times_ms[0] = t_compute;
-        a->times_ms[1] = (gather || pipelined || fused) ? t_gather : 0.f;
+        a->times_ms[1] = (gather || pipelined || fused || nvls) ? t_gather : 0.f;
     }
     return rc;
 }

@@ -63,6 +63,10 @@ struct TcParams {
     int l2_evict_last;       // 1: operand tiles are loaded with an L2 evict_last policy
     int npeers;
     __half* peer_c[kMaxPeers];
+    // fused all-gather through NVLS (XG = 2): the multicast address of C's first element (same ldc);
+    // every finished box is stored once there and the switch writes it into every member GPU's C,
+    // this GPU's included, so the local store is skipped
+    __half* mc_c;
     unsigned long long timeout_ns;
     // work units: full_units whole tiles and the tail tiles, each cut either into two column
     // halves (nsplit = 1: BN/2-wide MMAs, no reduction) or into `split` k-slices; the whole tiles
@@ -206,6 +210,34 @@ __device__ __forceinline__ void tmem_words_to_f32(const uint32_t (&r)[32], float
     }
 }
 
+// multimem store of 16 bytes to a multicast address: the NVSwitch replicates it into the same
+// offset of every member GPU's buffer.
+__device__ __forceinline__ void multimem_st_16(void* addr, const uint4& v)
+{
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Fused all-gather through NVLS: one warp stores its staged 32 x 32 fp16 box (row r's 64 bytes at
+// `pitch`) once to the multicast view of C, 4 lanes per row so each instruction writes 64-byte runs
+// of 8 rows.  The host guarantees N and ldc are multiples of 8 and the view is 16-byte aligned, so
+// every 16-byte segment with column < N is whole.
+__device__ __forceinline__ void store_box_multicast(const TcParams& p, const uint8_t* box, int pitch, int row0,
+                                                    int lane, int col)
+{
+    const int seg = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int rr = (lane >> 2) + 8 * j;
+        const int grow = row0 + rr;
+        const int gcol = col + seg * 8;
+        if (grow >= p.M || gcol >= p.N) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(box + rr * pitch + seg * 16);
+        multimem_st_16(p.mc_c + static_cast<long long>(grow) * p.ldc + gcol, v);
+    }
+}
+
 // Fused all-gather: one warp copies its staged 32 x 32 fp16 box (rows row0.., columns col..; row r's
 // 64 bytes at `pitch`, 16-byte chunk j at j ^ ((r >> 1) & 3) when `swizzled`) into every peer's C,
 // 4 lanes per row so each store instruction writes 64-byte runs of 8 rows.  Same bounds as the local
@@ -245,9 +277,11 @@ __device__ __forceinline__ void store_box_to_peers(const TcParams& p, const uint
 // alternate, and a buffer is rewritten only after the store issued from it two chunks earlier has
 // read it.  Otherwise each global store instruction writes 64-byte runs of 8 rows (4 lanes per row)
 // instead of 16 bytes of 32 different rows.
-// PEERS: compiled only into the kernel instance that serves vk_gemm_peers, so the default kernels'
-// epilogue code stays exactly as it is without peer stores.
-template <bool PEERS>
+// XG (exchange of C with other GPUs): 0 = none; 1 = the box is also stored into every peer's C
+// (vk_gemm_peers); 2 = the box is stored once to the multicast view of C instead of locally
+// (vk_gemm_mc; the host turns TMA stores off).  Each value is its own kernel instance, so the
+// default kernels' epilogue code stays exactly as it is without the exchange.
+template <int XG>
 __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap* tmap_c, uint8_t* stg, int row0,
                                            int lane, int col, float (&f)[32], uint32_t& nbuf)
 {
@@ -294,7 +328,7 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
             tma_store_2d(tmap_c, smem_u32(buf), col, row0);
             bulk_commit_group();
         }
-        if constexpr (PEERS) store_box_to_peers(p, buf, 64, true, row0, lane, col);
+        if constexpr (XG == 1) store_box_to_peers(p, buf, 64, true, row0, lane, col);
         ++nbuf;
         return;
     }
@@ -304,7 +338,12 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
         srow[j] = make_uint4(pack_half2(f[8 * j], f[8 * j + 1]), pack_half2(f[8 * j + 2], f[8 * j + 3]),
                              pack_half2(f[8 * j + 4], f[8 * j + 5]), pack_half2(f[8 * j + 6], f[8 * j + 7]));
     __syncwarp();
-    if constexpr (PEERS) store_box_to_peers(p, stg, kEpiPitch, false, row0, lane, col);
+    if constexpr (XG == 2) {
+        store_box_multicast(p, stg, kEpiPitch, row0, lane, col);
+        __syncwarp();
+        return;
+    }
+    if constexpr (XG == 1) store_box_to_peers(p, stg, kEpiPitch, false, row0, lane, col);
     const int seg = lane & 3;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -327,7 +366,7 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
     __syncwarp();
 }
 
-template <int CG, int BN, int STAGES, int KA, bool ACC_F32, bool PEERS = false>
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32, int XG = 0>
 __global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_c, const TcParams p)
@@ -682,7 +721,7 @@ __global__ void __launch_bounds__(192, 1)
                                     }
                                 }
                             }
-                            store_rows<PEERS>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                            store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                         }
                     } else if (ok) {
                         __threadfence();
@@ -751,7 +790,7 @@ __global__ void __launch_bounds__(192, 1)
                                         }
                                     }
                                 }
-                                store_rows<PEERS>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                                store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                             }
                             __syncwarp();
                         }
@@ -770,7 +809,7 @@ __global__ void __launch_bounds__(192, 1)
                     if (col0 + c < p.N) {
                         float f[32];
                         tmem_words_to_f32<ACC_F32>(r, f);
-                        store_rows<PEERS>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                        store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
                     }
                 }
             }
@@ -788,6 +827,8 @@ __global__ void __launch_bounds__(192, 1)
             }
         }
         if (p.c_tma && lane == 0) bulk_wait_group_all();  // C written before the CTA exits
+        // multicast stores are ordered at system scope before the kernel's completion is observed
+        if constexpr (XG == 2) asm volatile("fence.acq_rel.sys;" ::: "memory");
     }
 
     tc_fence_before();

@@ -459,13 +459,15 @@ struct Problem {
     // vk_gemm_peers: peer C buffers that also receive every finished box of C (tensor-core path only)
     int npeers = 0;
     void* peer_c[kMaxPeers] = {};
+    // vk_gemm_mc: multicast view of C (tensor-core path only; C itself is written through it)
+    void* mc_c = nullptr;
 };
 
-template <int CG, int BN, int STAGES, int KA, bool ACC_F32, bool PEERS = false>
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32, int XG = 0>
 static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScratch* fixed)
 {
     using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32>;
-    auto fn = tc_gemm_kernel<CG, BN, STAGES, KA, ACC_F32, PEERS>;
+    auto fn = tc_gemm_kernel<CG, BN, STAGES, KA, ACC_F32, XG>;
     int max_units = 0;
     int rc = kernel_slot(st, fn, Cfg::kSmemBytes, Cfg::kThreads, CG, &max_units);
     if (rc != VK_OK) return rc;
@@ -501,10 +503,12 @@ static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScr
         if (q < pb.npeers) peers_vec = peers_vec && reinterpret_cast<uintptr_t>(pb.peer_c[q]) % 16 == 0;
     }
     p.vec_ok = (c_vec && c32_vec && peers_vec) ? 1 : 0;
-    // TMA stores of C need a 16-byte aligned base and a pitch that is a multiple of 16 bytes
+    p.mc_c = static_cast<__half*>(pb.mc_c);
+    // TMA stores of C need a 16-byte aligned base and a pitch that is a multiple of 16 bytes; with a
+    // multicast view every box goes through it instead of a local store
     CUtensorMap tc;
     memset(&tc, 0, sizeof(tc));
-    p.c_tma = (g_tma_store.load(std::memory_order_relaxed) && c_vec && pb.m > 0 && pb.n > 0 &&
+    p.c_tma = (XG != 2 && g_tma_store.load(std::memory_order_relaxed) && c_vec && pb.m > 0 && pb.n > 0 &&
                pb.ldc * 2 < (1LL << 40)) ? 1 : 0;
     if (p.c_tma) {
         rc = cached_tmap(st, 1, &tc, pb.C, pb.m, pb.n, pb.ldc, 32, 32);
@@ -577,10 +581,18 @@ template <bool F32>
 static int launch_tc_variant(DeviceState& st, int dev, const Problem& pb, int algo, const FixedScratch* fixed)
 {
     const int tn = pb.tile_n ? pb.tile_n : 256;
+    if (pb.mc_c != nullptr) {
+        // the multicast epilogue is compiled into the default pair kernel only
+        if (algo == VK_ALGO_TC_2SM && tn == 256 && g_bk_2sm256.load(std::memory_order_relaxed) == 128)
+            return launch_tc<2, 256, 3, 2, F32, 2>(st, dev, pb, fixed);
+        return set_error(VK_ERR_UNSUPPORTED,
+                         "vk_gemm_mc: multicast stores run on the default pair kernel only (algo AUTO or TC_2SM, "
+                         "tile_n 256, bk_2sm256 128)");
+    }
     if (pb.npeers > 0) {
         // the peer-storing epilogue is compiled into the default pair kernel only
         if (algo == VK_ALGO_TC_2SM && tn == 256 && g_bk_2sm256.load(std::memory_order_relaxed) == 128)
-            return launch_tc<2, 256, 3, 2, F32, true>(st, dev, pb, fixed);
+            return launch_tc<2, 256, 3, 2, F32, 1>(st, dev, pb, fixed);
         return set_error(VK_ERR_UNSUPPORTED,
                          "vk_gemm_peers: peer stores run on the default pair kernel only (algo AUTO or TC_2SM, "
                          "tile_n 256, bk_2sm256 128)");
@@ -745,7 +757,7 @@ void release_device_state()
 using namespace vk;
 
 static int gemm_entry(const vk_gemm_args* a, const vk_gemm_ext* x, const char* name, void* const* peers = nullptr,
-                      int npeers = 0)
+                      int npeers = 0, void* mc_c = nullptr)
 {
     if (a == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "%s: args is NULL", name);
     if (a->m < 0 || a->n < 0 || a->k < 0)
@@ -826,6 +838,23 @@ static int gemm_entry(const vk_gemm_args* a, const vk_gemm_ext* x, const char* n
     DeviceState* st = nullptr;
     int rc = current_device(&dev, &st);
     if (rc != VK_OK) return rc;
+    if (mc_c != nullptr) {
+        if (a->dtype != VK_DTYPE_F16)
+            return set_error(VK_ERR_UNSUPPORTED, "%s: multicast stores are for the fp16 tensor-core kernels", name);
+        if (pb.n % 8 != 0 || pb.ldc % 8 != 0 || reinterpret_cast<uintptr_t>(pb.C) % 16 != 0 ||
+            reinterpret_cast<uintptr_t>(mc_c) % 16 != 0)
+            return set_error(VK_ERR_ALIGNMENT, "%s: needs n and ldc multiples of 8 and 16-byte aligned C and C_mc",
+                             name);
+        // C_mc must be the multicast view of exactly this C (same offset inside a live team's buffer)
+        if (pb.m > 0 && pb.n > 0) {
+            const size_t extent = static_cast<size_t>((pb.m - 1) * pb.ldc + pb.n) * 2;
+            if (mc_lookup(dev, pb.C, extent) != mc_c)
+                return set_error(VK_ERR_INVALID_ARGUMENT,
+                                 "%s: C is not inside a multicast buffer of this device, or C_mc is not its "
+                                 "multicast view", name);
+        }
+        pb.mc_c = mc_c;
+    }
     return dispatch(*st, dev, pb, a->dtype, a->acc, a->algo);
 }
 
@@ -838,6 +867,12 @@ extern "C" int vk_gemm_peers(const vk_gemm_args* a, void* const* peer_C, int32_t
     return gemm_entry(a, nullptr, "vk_gemm_peers", peer_C, npeers);
 }
 
+extern "C" int vk_gemm_mc(const vk_gemm_args* a, void* C_mc)
+{
+    if (C_mc == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm_mc: C_mc is NULL");
+    return gemm_entry(a, nullptr, "vk_gemm_mc", nullptr, 0, C_mc);
+}
+
 namespace vk {
 int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc, int algo_in)
 {
@@ -846,6 +881,8 @@ int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc
     if (pb.C == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: C is NULL");
     if (pb.npeers > 0 && (pb.k == 0 || algo_in == VK_ALGO_SIMT || algo_in == VK_ALGO_FFMA))
         return set_error(VK_ERR_UNSUPPORTED, "vk_gemm_peers: peer stores need the tensor-core kernels and k > 0");
+    if (pb.mc_c != nullptr && (pb.k == 0 || algo_in == VK_ALGO_SIMT || algo_in == VK_ALGO_FFMA))
+        return set_error(VK_ERR_UNSUPPORTED, "vk_gemm_mc: multicast stores need the tensor-core kernels and k > 0");
     if (pb.k == 0) return dtype == VK_DTYPE_F16 ? launch_zero<__half>(*st, pb) : launch_zero<float>(*st, pb);
     if (pb.A == nullptr || pb.B == nullptr) return set_error(VK_ERR_INVALID_ARGUMENT, "vk_gemm: A or B is NULL");
 
@@ -892,7 +929,7 @@ int dispatch(DeviceState& st_ref, int dev, const Problem& pb, int dtype, int acc
                                  : launch_tc_variant<false>(*st, dev, pk, VK_ALGO_TC_2SM, nullptr);
     }
     if (algo == VK_ALGO_AUTO) algo = tma_ok ? VK_ALGO_TC_2SM : VK_ALGO_SIMT;
-    if (algo == VK_ALGO_SIMT && pb.npeers > 0)
+    if (algo == VK_ALGO_SIMT && (pb.npeers > 0 || pb.mc_c != nullptr))
         return set_error(VK_ERR_UNSUPPORTED,
                          "vk_gemm_peers: these operands need the predicated kernel (enable \"repack\"), which has no "
                          "peer stores");

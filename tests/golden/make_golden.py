@@ -3,7 +3,11 @@
 Run where the reference tree is available (it builds ``oracle/_ref`` from the reference's
 unmodified v0 sources first):
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle && python tests/golden/make_golden.py [case names; default: all]
+
+The reference's OpenBLAS selects its sgemm kernel by CPU model; ``oracle/v0.py`` pins the kernel the
+fixtures were made with ("Cooperlake", AVX-512 BF16) wherever the CPU can run it, so regenerating
+them on such a CPU reproduces the committed files bit for bit.
 
 Each fixture is an ``.npz`` holding the seeded-input recipe, sha256 digests of the
 generated inputs (so a drift of the generator is caught before any comparison), the
@@ -31,6 +35,8 @@ CASES = [
     ("cfg2_4096_seed2", 4096, 4096, 4096, 2, "uniform", -0.5, 0.5, "f16", 128),
     ("cfg3_sgemm_1024_seed3", 1024, 1024, 1024, 3, "normal", 0.0, 0.0, "f32", 32),
     ("cfg5_ragged_4000x5120x3000_seed5", 4000, 5120, 3000, 5, "uniform", -1.0, 1.0, "f16", 125),
+    ("cfg3_sgemm_4096_seed3", 4096, 4096, 4096, 3, "normal", 0.0, 0.0, "f32", 128),
+    ("cfg4a_16384_seed4", 16384, 16384, 16384, 4, "uniform", -1.0, 1.0, "f16", 512),
     ("tiny_1x1x1", 1, 1, 1, 11, "uniform", -1.0, 1.0, "f16", 1),
     ("tiny_7x13x5", 7, 13, 5, 12, "uniform", -1.0, 1.0, "f16", 1),
     ("ragged_200x136x72", 200, 136, 72, 13, "uniform", -1.0, 1.0, "f16", 1),
@@ -43,8 +49,10 @@ def sha(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
-def main() -> None:
+def main(names: list[str]) -> None:
     for name, m, n, k, seed, dist, lo, hi, dt, stride in CASES:
+        if names and name not in names:
+            continue
         dtype = np.float16 if dt == "f16" else np.float32
         A, B = v0.make_inputs(m, n, k, seed, dist, lo, hi, dtype)
         rows = np.arange(0, m, stride, dtype=np.int64)
@@ -60,4 +68,4 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

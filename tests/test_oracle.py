@@ -13,9 +13,12 @@ import pytest
 
 from oracle import v0
 
-GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+ALL_GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.npz")))
+# The 16384^3 fixture (1 GiB of inputs) gets one test of its own that generates its inputs once.
+BIG = [g for g in ALL_GOLDEN if "16384" in os.path.basename(g)]
+GOLDEN = [g for g in ALL_GOLDEN if g not in BIG]
 # Cases small enough to regenerate in well under a second each on one core.
-FAST = [g for g in GOLDEN if "4096" not in os.path.basename(g) and "4000x5120" not in os.path.basename(g)]
+FAST = [g for g in GOLDEN if not any(t in os.path.basename(g) for t in ("4096", "4000x5120", "16384"))]
 
 
 def _load(path):
@@ -33,7 +36,24 @@ def _sha(a):
 def test_fixtures_present():
     names = {os.path.basename(g) for g in GOLDEN}
     assert "cfg0_1024_seed0.npz" in names and "cfg5_ragged_4000x5120x3000_seed5.npz" in names
-    assert len(GOLDEN) >= 10
+    assert len(GOLDEN) >= 10 and len(BIG) == 1
+
+
+@pytest.mark.parametrize("path", BIG, ids=[os.path.basename(g) for g in BIG])
+def test_big_fixture(path):
+    """configs[4a] (16384^3, seed 4): input digests, the restatement and the compiled reference."""
+    from vibekernel_b200 import testdata  # same recipe as v0.make_inputs (tests/test_testdata.py), chunked
+    z = np.load(path)
+    A, B = testdata.make_inputs(int(z["m"]), int(z["n"]), int(z["k"]), int(z["seed"]), str(z["dist"]),
+                                float(z["lo"]), float(z["hi"]), np.float16)
+    assert _sha(A) == str(z["sha_A"]) and _sha(B) == str(z["sha_B"]), "input generator drifted"
+    rows = z["rows"]
+    gold = z["C"]
+    c16, c32 = v0.v0_f16(A[rows], B)
+    assert np.mean(c16.view(np.uint16) != gold.view(np.uint16)) < 0.01
+    assert v0.max_elem_rel(c16, gold) < 2e-3
+    if v0.ref_available() and v0.coretype_pinned():
+        assert np.array_equal(v0.ref_v0_f16(A[rows], B).view(np.uint16), gold.view(np.uint16))
 
 
 @pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(g) for g in GOLDEN])

@@ -47,7 +47,7 @@ def test_sharded_single_gpu_no_exchange(vk):
 
 
 @pytest.mark.parametrize("m", [4096, 4001])  # even split (ncclAllGather) / uneven (broadcasts)
-@pytest.mark.parametrize("mode", [True, "pipelined", "fused"], ids=["nccl", "pipelined", "fused"])
+@pytest.mark.parametrize("mode", [True, "pipelined", "fused"], ids=["nccl", "pipelined", "fused"])  # nvls: test_nvls_gpu.py
 def test_sharded_multi_gpu_allgather(vk, m, mode):
     ngpu = torch.cuda.device_count()
     if ngpu < 2:
@@ -74,13 +74,17 @@ def test_sharded_multi_gpu_local_blocks_only(vk):
         assert np.isnan(outside.astype(np.float32)).all(), "a GPU wrote outside its row block"
 
 
-def test_torchrun_two_ranks(vk):
-    if torch.cuda.device_count() < 2:
+@pytest.mark.parametrize("big", [False, True], ids=["shapes", "cfg4a_16384"])
+def test_torchrun_all_gpus(vk, big):
+    """One rank per visible GPU: every gather mode (NCCL, copy engines, fused peer stores, NVLS), and
+    BASELINE configs[4a] at full size."""
+    ngpu = torch.cuda.device_count()
+    if ngpu < 2:
         pytest.skip("needs >= 2 GPUs")
     env = dict(os.environ, PYTHONPATH=ROOT)
-    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", "29731",
-           os.path.join(ROOT, "tests", "_dist_gpu_worker.py")]
+    cmd = ["timeout", "-k", "30", "420", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", str(ngpu), "--master-addr", "127.0.0.1", "--master-port", "29731" if big else "29733",
+           os.path.join(ROOT, "tests", "_dist_gpu_worker.py")] + (["--big"] if big else [])
     res = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
     assert "rank0 ok" in res.stdout

@@ -40,7 +40,8 @@ EXPORTED = (
     "vk_last_error_string", "vk_version_string", "vk_device_error", "vk_selftest_wait_timeout",
     "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
     "vk_gemm_host", "vk_gemm_ex", "vk_read_trace_cta", "vk_ipc_export", "vk_ipc_import", "vk_ipc_release",
-    "vk_copy_async", "vk_debug_schedule", "vk_gemm_peers",
+    "vk_copy_async", "vk_debug_schedule", "vk_gemm_peers", "vk_gemm_mc", "vk_mc_supported", "vk_mc_alloc",
+    "vk_mc_free", "vk_mc_create", "vk_mc_import", "vk_mc_attach", "vk_mc_detach",
 )
 
 
@@ -101,6 +102,23 @@ def _load() -> ctypes.CDLL:
     lib.vk_gemm_ex.restype = ctypes.c_int
     lib.vk_gemm_peers.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32]
     lib.vk_gemm_peers.restype = ctypes.c_int
+    lib.vk_gemm_mc.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_void_p]
+    lib.vk_gemm_mc.restype = ctypes.c_int
+    vpp = ctypes.POINTER(ctypes.c_void_p)
+    lib.vk_mc_supported.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+    lib.vk_mc_supported.restype = ctypes.c_int
+    lib.vk_mc_alloc.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_size_t, vpp, vpp]
+    lib.vk_mc_alloc.restype = ctypes.c_int
+    lib.vk_mc_free.argtypes = [ctypes.c_void_p]
+    lib.vk_mc_free.restype = ctypes.c_int
+    lib.vk_mc_create.argtypes = [ctypes.c_int, ctypes.c_int32, ctypes.c_size_t, vpp, ctypes.POINTER(ctypes.c_int64)]
+    lib.vk_mc_create.restype = ctypes.c_int
+    lib.vk_mc_import.argtypes = [ctypes.c_int, ctypes.c_int32, ctypes.POINTER(ctypes.c_int64), vpp]
+    lib.vk_mc_import.restype = ctypes.c_int
+    lib.vk_mc_attach.argtypes = [ctypes.c_void_p, vpp, vpp, ctypes.POINTER(ctypes.c_size_t)]
+    lib.vk_mc_attach.restype = ctypes.c_int
+    lib.vk_mc_detach.argtypes = [ctypes.c_void_p]
+    lib.vk_mc_detach.restype = ctypes.c_int
     sz = ctypes.c_size_t
     lib.vk_matmul_f16.argtypes = [ctypes.c_int, sz, sz, sz, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.vk_matmul_f16.restype = ctypes.c_int
@@ -185,7 +203,8 @@ def _row_pitch(t) -> int:
 def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile_n: int = 0,
          stream=None, lda: int = 0, ldb: int = 0, ldc: int = 0, m: int | None = None,
          n: int | None = None, k: int | None = None, trans_a: bool = False, trans_b: bool = False,
-         alpha: float = 1.0, beta: float = 0.0, c_in=None, bias=None, act: str | None = None, peers=None):
+         alpha: float = 1.0, beta: float = 0.0, c_in=None, bias=None, act: str | None = None, peers=None,
+         mc: int | None = None):
     """C = act(alpha * op(A) @ op(B) + beta * c_in + bias) on the GPU (``vk_gemm`` / ``vk_gemm_ex``).
 
     A is [m, k] (or [k, m] with ``trans_a``) and B is [k, n] (or [n, k] with ``trans_b``), CUDA
@@ -195,6 +214,9 @@ def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile
     or "relu".  Asynchronous on ``stream`` (default: torch's current stream).  ``peers``: addresses (ints)
     or tensors of up to 7 peer buffers that also receive C, box by box, at the same row / column offsets
     and ldc (``vk_gemm_peers``: the fused all-gather; fp16 tensor-core path, no epilogue extensions).
+    ``mc``: address of the multicast view of C (``vk_gemm_mc``: C lies in a multicast buffer, see
+    :class:`McBuffer` and ``dist_gemm.McRowGather``; every box is stored once through the NVSwitch into
+    all member GPUs' C).
     """
     import torch
     if A.dtype not in (torch.float16, torch.float32) or B.dtype != A.dtype:
@@ -227,6 +249,11 @@ def gemm(A, B, C=None, *, acc: str = "f32", algo: str = "auto", c_f32=None, tile
     a.stream = _stream_handle(stream)
     extended = trans_a or trans_b or alpha != 1.0 or beta != 0.0 or bias is not None or act is not None
     with torch.cuda.device(A.device):
+        if mc is not None:
+            if extended or peers:
+                raise ValueError("mc cannot be combined with peers, transposes or the fused epilogue")
+            check(lib.vk_gemm_mc(ctypes.byref(a), ctypes.c_void_p(int(mc))))
+            return C
         if peers is not None and len(peers) > 0:
             if extended:
                 raise ValueError("peers cannot be combined with transposes or the fused epilogue")
@@ -374,8 +401,10 @@ def gemm_sharded(A_parts, B_parts, C_parts, m: int, n: int, k: int, *, acc: str 
 
     A_parts[r]: GPU r's row slice [rows_r, k]; B_parts[r]: full [k, n] on GPU r; C_parts[r]: full
     [m, n] buffer on GPU r.  ``allgather``: False, True (NCCL after the GEMMs), "pipelined" (peer
-    copies of finished row chunks overlapped with the GEMM) or "fused" (every GPU's epilogue also
-    stores its C boxes into all peers' C).  Returns (compute_ms, gather_ms), each the max over GPUs.
+    copies of finished row chunks overlapped with the GEMM), "fused" (every GPU's epilogue also
+    stores its C boxes into all peers' C) or "nvls" (C_parts are the views of one :class:`McBuffer`;
+    every GPU's epilogue stores each box once to the multicast view).  Returns (compute_ms,
+    gather_ms), each the max over GPUs.
     """
     import torch
     g = len(A_parts)
@@ -392,10 +421,63 @@ def gemm_sharded(A_parts, B_parts, C_parts, m: int, n: int, k: int, *, acc: str 
     s.dtype = DTYPE_F16 if A_parts[0].dtype == torch.float16 else DTYPE_F32
     s.acc = _ACCS[acc]
     s.algo = _ALGOS[algo]
-    s.allgather_c = {"pipelined": 2, "fused": 3}.get(allgather, 1 if allgather else 0)
+    s.allgather_c = {"pipelined": 2, "fused": 3, "nvls": 4}.get(allgather, 1 if allgather else 0)
     s.times_ms = times
     check(lib.vk_gemm_sharded(ctypes.byref(s)))
     return float(times[0]), float(times[1])
+
+
+# ------------------------------------------------------------------------------------------
+# NVLS multicast buffers
+# ------------------------------------------------------------------------------------------
+def mc_supported(device: int = 0) -> bool:
+    """True when ``device`` supports NVLink SHARP multicast (an NVSwitch system)."""
+    v = ctypes.c_int(0)
+    check(lib.vk_mc_supported(device, ctypes.byref(v)))
+    return bool(v.value)
+
+
+class _CudaArray:
+    """__cuda_array_interface__ wrapper: lets torch view device memory the library mapped itself."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+def _view(ptr: int, shape, dtype, device):
+    import torch
+    typestr = {torch.float16: "<f2", torch.float32: "<f4"}[dtype]
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device=device)
+
+
+class McBuffer:
+    """One multicast buffer over several GPUs of this process (``vk_mc_alloc``).
+
+    ``views[i]`` is a [rows, cols] tensor in GPU ``devices[i]``'s own memory; ``mc`` is the address
+    of the multicast view.  Free with :meth:`free` after every GPU is done with it.
+    """
+
+    def __init__(self, devices, rows: int, cols: int, dtype):
+        import torch
+        esize = torch.tensor([], dtype=dtype).element_size()
+        g = len(devices)
+        devs = (ctypes.c_int32 * g)(*devices)
+        ptrs = (ctypes.c_void_p * g)()
+        mc = ctypes.c_void_p()
+        check(lib.vk_mc_alloc(g, devs, rows * cols * esize, ptrs, ctypes.byref(mc)))
+        self.devices = list(devices)
+        self.mc = int(mc.value)
+        self.views = [_view(ptrs[i], (rows, cols), dtype, torch.device("cuda", d)) for i, d in enumerate(devices)]
+
+    def free(self) -> None:
+        if self.mc:
+            import torch
+            for d in self.devices:
+                torch.cuda.synchronize(d)
+            self.views = []
+            check(lib.vk_mc_free(ctypes.c_void_p(self.mc)))
+            self.mc = 0
 
 
 def ipc_export(tensor) -> bytes:

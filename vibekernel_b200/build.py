@@ -19,7 +19,7 @@ ROOT = os.path.dirname(HERE)
 # scan (it walks task-1/src and task-1/include) covers every kernel.
 CSRC = os.path.join(ROOT, "task-1", "src", "vkgemm")
 LIB = os.path.join(HERE, "libvkgemm.so")
-SOURCES = ["vkgemm.cu", "sharded.cu", "host_gemm.cu", "peer_ipc.cu"]
+SOURCES = ["vkgemm.cu", "sharded.cu", "host_gemm.cu", "peer_ipc.cu", "nvls.cu"]
 DEPS = SOURCES + ["ptx.cuh", "tc_gemm.cuh", "simt_gemm.cuh", "vk_internal.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -10,7 +10,10 @@ so each rank's block is one contiguous span.  Two ways:
     finishes, pushes it into every peer's C with the copy engines (no SMs taken from the GEMM)
     while the next chunk is computed.  Mode "fused": one GEMM whose epilogue stores every finished
     box of C into the peers' C as well (vk_gemm_peers, plain stores over NVLink).  Either way a
-    one-element all-reduce at the end completes on every rank only after every rank's stores have.
+    one-element all-reduce at the end completes on every rank only after every rank's stores have;
+  * ``McRowGather``: NVLink SHARP.  C_full is one multicast buffer over all ranks (each rank's view
+    is its own memory); the GEMM epilogue stores every finished box once to the multicast view of
+    its rows (vk_gemm_mc) and the NVSwitch writes it into every rank's C_full.
 The reference has no multi-GPU path (README.md:161); this is the layer BASELINE.json asks for.
 """
 from __future__ import annotations
@@ -117,6 +120,87 @@ class PeerRowGather:
         for ptr in self.peers.values():
             ipc_release(ptr)
         self.peers = {}
+
+
+class McRowGather:
+    """All-gather of C row blocks fused into the GEMM through an NVLS multicast buffer (one process
+    per GPU, NVSwitch systems: ``vibekernel_b200.mc_supported``).
+
+    Collective: every rank constructs it with the same (m, n, off), calls ``run`` the same number of
+    times and ``close`` exactly once (also on error paths), because a rank must not leave while its
+    memory is bound to the multicast object and the others may still store into it.  ``C_full`` is
+    this rank's view, a [m, n] tensor in its own memory.
+    """
+
+    def __init__(self, m: int, n: int, off, rank: int, dtype=None, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _view, check, lib
+        dtype = dtype or torch.float16
+        self.off, self.rank, self.group = list(off), rank, group
+        world = len(off) - 1
+        dev = torch.cuda.current_device()
+        esize = torch.tensor([], dtype=dtype).element_size()
+        team = ctypes.c_void_p()
+        share = (ctypes.c_int64 * 3)()
+        status = ""
+        if rank == 0:
+            rc = lib.vk_mc_create(dev, world, m * n * esize, ctypes.byref(team), share)
+            status = "" if rc == 0 else f"rank 0: {_err_text(rc)}"
+        obj = [(status, list(share))]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group else 0, group=group)
+        status, shared = obj[0]
+        if not status and rank != 0:
+            rc = lib.vk_mc_import(dev, world, (ctypes.c_int64 * 3)(*shared), ctypes.byref(team))
+            status = "" if rc == 0 else f"rank {rank}: {_err_text(rc)}"
+        # every member must have the object before any member binds memory (binding waits for all)
+        statuses = [None] * world
+        dist.all_gather_object(statuses, status, group=group)
+        failed = [s for s in statuses if s]
+        if failed:
+            if team.value:
+                lib.vk_mc_detach(team)
+            raise RuntimeError("multicast buffer setup failed: " + "; ".join(failed))
+        local, mc, size = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_size_t()
+        check(lib.vk_mc_attach(team, ctypes.byref(local), ctypes.byref(mc), ctypes.byref(size)))
+        dist.barrier(group=group)  # every member bound before anyone stores through the multicast view
+        self._team = team
+        self.mc = int(mc.value)
+        self.row_bytes = n * esize
+        self.C_full = _view(local.value, (m, n), dtype, torch.device("cuda", dev))
+        self.flag = torch.zeros(1, dtype=torch.float32, device=self.C_full.device)
+
+    def run(self, A_local, B, gemm):
+        """``gemm(A_local, B, C_rows, mc=...)`` for this rank's rows; returns (stream order) once every
+        rank's C_full is complete."""
+        import torch.distributed as dist
+        lo, hi = self.off[self.rank], self.off[self.rank + 1]
+        if hi > lo:
+            gemm(A_local, B, self.C_full[lo:hi], mc=self.mc + lo * self.row_bytes)
+        dist.all_reduce(self.flag, group=self.group)
+        return self.C_full
+
+    def close(self) -> None:
+        import torch
+        import torch.distributed as dist
+
+        from . import check, lib
+        if self._team is None:
+            return
+        torch.cuda.synchronize(self.C_full.device)
+        dist.barrier(group=self.group)  # nobody stores into or reads the buffer any more
+        self.C_full = None
+        team, self._team = self._team, None
+        check(lib.vk_mc_detach(team))
+        dist.barrier(group=self.group)  # nobody leaves while another member is still bound
+
+
+def _err_text(rc: int) -> str:
+    from . import last_error
+    return f"vkgemm error {rc}: {last_error()}"
 
 
 def sharded_matmul(A_local, B, C_full, off, rank: int, gemm, allgather: bool = True, group=None):
