@@ -273,6 +273,9 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *   "bk_2sm256"       k per pipeline stage of the 256-column pair kernel: 128 (default, 3 stages
  *                     of 64 KB) or 64 (6 stages of 32 KB)
  *   "wait_timeout_ns" same as vk_set_wait_timeout_ns
+ *   "gather_timeout_ms" host-side deadline of vk_gemm_sharded's NCCL all-gather (60000): when it passes,
+ *                     or NCCL reports an asynchronous error, the communicators are aborted
+ *                     (ncclCommAbort) and the call returns VK_ERR_NCCL instead of waiting forever
  *   "repack"          1 (default) = VK_ALGO_AUTO copies an fp16 operand whose pitch or base breaks the
  *                     TMA rule into a 16-byte-pitched scratch buffer (cached per stream) and runs the
  *                     tensor-core kernel; 0 = such problems run on the predicated CUDA-core kernel
@@ -297,6 +300,13 @@ int vk_set_option(const char* name, int64_t value);
  * max_units_out units) = {tile, first k-block, end k-block, slice index | 100 + column half | -1}. */
 int vk_debug_schedule(int64_t tiles, int32_t num_kb, int32_t max_units, int64_t k, int32_t flags,
                       int32_t* out_plan, int32_t* out_units, int32_t max_units_out);
+
+/* Test hook (no counterpart in the reference; touches no device): runs the host-side watchdog that
+ * guards vk_gemm_sharded's NCCL all-gather against a fake completion query that reports "done" after
+ * `done_after_polls` polls (< 0: never) or "failed" at poll `fail_at_poll` (<= 0: never).  *aborted counts
+ * the abort calls, *polls the queries.  Returns VK_OK or VK_ERR_NCCL like the real gather. */
+int vk_debug_watchdog(int64_t deadline_ms, int32_t done_after_polls, int32_t fail_at_poll, int32_t* aborted,
+                      int64_t* polls);
 
 /* Clock probe (no counterpart in the reference, whose scores were confounded by the unlogged
  * SM clock, README.md:160): out3 = {SM cycles, nanoseconds, launches} accumulated since the last

@@ -10,7 +10,10 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <functional>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "vkgemm.h"
@@ -29,6 +32,8 @@ struct NcclApi {
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 NcclApi g_nccl;
@@ -48,6 +53,8 @@ int load_nccl()
     bool ok = bind(h, "ncclCommInitAll", g_nccl.CommInitAll) && bind(h, "ncclAllGather", g_nccl.AllGather) &&
               bind(h, "ncclBroadcast", g_nccl.Broadcast) && bind(h, "ncclGroupStart", g_nccl.GroupStart) &&
               bind(h, "ncclGroupEnd", g_nccl.GroupEnd) && bind(h, "ncclCommDestroy", g_nccl.CommDestroy) &&
+              bind(h, "ncclCommAbort", g_nccl.CommAbort) &&
+              bind(h, "ncclCommGetAsyncError", g_nccl.CommGetAsyncError) &&
               bind(h, "ncclGetErrorString", g_nccl.GetErrorString);
     if (!ok) return vk::set_error(VK_ERR_NCCL, "libnccl.so.2 lacks an expected symbol");
     g_nccl.loaded = true;
@@ -150,7 +157,53 @@ int ensure_comms(ShardGroup* g)
     return VK_OK;
 }
 
+// Host-side watchdog of an enqueued collective: polls `query` (1 = complete, 0 = still running,
+// -1 = failed) until it completes or `deadline_ms` passes; on a failure or at the deadline it calls
+// `abort` once (ncclCommAbort on the real path, which makes the in-flight NCCL kernels give up) and
+// returns VK_ERR_NCCL.  A rank that never joins the gather therefore costs the caller an error after
+// the deadline instead of a hang.
+int watch_collective(const std::function<int()>& query, const std::function<void()>& abort, long long deadline_ms,
+                     const char* what, long long* polls_out)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    long long polls = 0;
+    int state = 0;
+    while (true) {
+        state = query();
+        ++polls;
+        if (state != 0) break;
+        const long long waited =
+            std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (waited >= deadline_ms) break;
+        std::this_thread::sleep_for(std::chrono::microseconds(polls < 64 ? 5 : 100));
+    }
+    if (polls_out) *polls_out = polls;
+    if (state == 1) return VK_OK;
+    abort();
+    if (state < 0) return vk::set_error(VK_ERR_NCCL, "%s failed; communicators aborted", what);
+    return vk::set_error(VK_ERR_NCCL, "%s did not complete within %lld ms; communicators aborted", what, deadline_ms);
+}
+
 }  // namespace
+
+extern "C" int vk_debug_watchdog(int64_t deadline_ms, int32_t done_after_polls, int32_t fail_at_poll, int32_t* aborted,
+                                 int64_t* polls)
+{
+    if (deadline_ms < 0 || aborted == nullptr) return vk::set_error(VK_ERR_INVALID_ARGUMENT, "vk_debug_watchdog: bad args");
+    *aborted = 0;
+    long long n = 0;
+    auto query = [&]() {
+        ++n;
+        if (fail_at_poll > 0 && n >= fail_at_poll) return -1;
+        if (done_after_polls >= 0 && n > done_after_polls) return 1;
+        return 0;
+    };
+    auto abort = [&]() { ++*aborted; };
+    long long p = 0;
+    const int rc = watch_collective(query, abort, deadline_ms, "fake collective", &p);
+    if (polls) *polls = p;
+    return rc;
+}
 
 extern "C" int vk_gemm_sharded(const vk_shard_args* a)
 {
@@ -317,6 +370,32 @@ extern "C" int vk_gemm_sharded(const vk_shard_args* a)
                 if (q != r) cudaStreamWaitEvent(g->streams[r], g->ev_compute[q], 0);
         }
         cudaEventRecord(g->ev_gather[r], g->streams[r]);
+    }
+    if (rc == VK_OK && gather) {
+        // NCCL gather under a deadline: every GPU's gather-done event, and no communicator error
+        auto query = [&]() {
+            int done = 1;
+            for (int r = 0; r < n_gpu; ++r) {
+                cudaSetDevice(a->devices[r]);
+                const cudaError_t q = cudaEventQuery(g->ev_gather[r]);
+                if (q == cudaErrorNotReady) {
+                    done = 0;
+                } else if (q != cudaSuccess) {
+                    return -1;
+                }
+                ncclResult_t ae = ncclSuccess;
+                if (g_nccl.CommGetAsyncError(g->comms[r], &ae) != ncclSuccess || ae != ncclSuccess) return -1;
+            }
+            return done;
+        };
+        auto abort = [&]() {
+            for (ncclComm_t c : g->comms) g_nccl.CommAbort(c);
+            g->comms.clear();  // the next call builds new communicators
+        };
+        rc = watch_collective(query, abort, vk::gather_timeout_ms(), "NCCL all-gather of C", nullptr);
+    }
+    for (int r = 0; r < n_gpu; ++r) {
+        cudaSetDevice(a->devices[r]);
         e = cudaStreamSynchronize(g->streams[r]);
         if (e != cudaSuccess && rc == VK_OK) rc = cuda_err(e, "shard synchronize");
         if (rc == VK_OK) {

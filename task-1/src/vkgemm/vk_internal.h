@@ -16,4 +16,6 @@ void release_host_pipes();
 // Multicast view of [ptr, ptr + bytes) on device `dev` when that range lies inside the unicast view of
 // a live multicast team (vk_mc_alloc / vk_mc_attach), else nullptr.
 void* mc_lookup(int dev, const void* ptr, size_t bytes);
+// Host-side deadline of the NCCL all-gather in vk_gemm_sharded, milliseconds (option "gather_timeout_ms").
+long long gather_timeout_ms();
 }  // namespace vk

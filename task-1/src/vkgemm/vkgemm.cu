@@ -147,6 +147,9 @@ static std::atomic<int> g_sgemm_v2{1};
 static std::atomic<int> g_sgemm_paired{1};
 static std::atomic<int> g_repack{1};
 static std::atomic<int> g_clock_probe_on{0};
+// Deadline of the NCCL all-gather in vk_gemm_sharded (after it, the communicators are aborted).
+static std::atomic<long long> g_gather_timeout_ms{60000};
+long long gather_timeout_ms() { return g_gather_timeout_ms.load(std::memory_order_relaxed); }
 // Devices (bit per ordinal < 31) on which each SGEMM variant's shared-memory attribute is set.
 static std::atomic<int> g_sgemm_attr_mask[3] = {{0}, {0}, {0}};
 static std::atomic<int> g_trace_on{0};
@@ -1184,6 +1187,11 @@ extern "C" int vk_set_option(const char* name, int64_t value)
     }
     if (strcmp(name, "clock_probe") == 0) {
         g_clock_probe_on.store(value != 0 ? 1 : 0);
+        return VK_OK;
+    }
+    if (strcmp(name, "gather_timeout_ms") == 0) {
+        if (value <= 0) return set_error(VK_ERR_INVALID_ARGUMENT, "gather_timeout_ms must be > 0");
+        g_gather_timeout_ms.store(value);
         return VK_OK;
     }
     if (strcmp(name, "wait_timeout_ns") == 0) {

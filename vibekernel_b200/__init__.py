@@ -41,7 +41,7 @@ EXPORTED = (
     "vk_set_wait_timeout_ns", "vk_set_option", "vk_read_clock_probe", "vk_read_trace", "vk_gemm_noalloc",
     "vk_gemm_host", "vk_gemm_ex", "vk_read_trace_cta", "vk_ipc_export", "vk_ipc_import", "vk_ipc_release",
     "vk_copy_async", "vk_debug_schedule", "vk_gemm_peers", "vk_gemm_mc", "vk_mc_supported", "vk_mc_alloc",
-    "vk_mc_free", "vk_mc_create", "vk_mc_import", "vk_mc_attach", "vk_mc_detach",
+    "vk_mc_free", "vk_mc_create", "vk_mc_import", "vk_mc_attach", "vk_mc_detach", "vk_debug_watchdog",
 )
 
 
@@ -160,6 +160,9 @@ def _load() -> ctypes.CDLL:
     lib.vk_debug_schedule.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
                                       i32p, i32p, ctypes.c_int32]
     lib.vk_debug_schedule.restype = ctypes.c_int
+    lib.vk_debug_watchdog.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, i32p,
+                                      ctypes.POINTER(ctypes.c_int64)]
+    lib.vk_debug_watchdog.restype = ctypes.c_int
     return lib
 
 
