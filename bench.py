@@ -132,24 +132,6 @@ class ClockSampler:
         if self._handle is not None:
             self._thread.join()
 
-    def nvlink_kib(self):
-        """(TX, RX) NVLink data counters of this GPU summed over its links, KiB; None if unavailable."""
-        if self._handle is None:
-            return None
-        try:
-            nv = self._nv
-            ids = [(nv.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX, link) for link in range(18)] + \
-                  [(nv.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX, link) for link in range(18)]
-            vals = nv.nvmlDeviceGetFieldValues(self._handle, ids)
-            ok = [v.nvmlReturn == 0 for v in vals]
-            if not any(ok):
-                return None
-            tx = sum(int(v.value.ullVal) for v, g in zip(vals[:18], ok[:18]) if g)
-            rx = sum(int(v.value.ullVal) for v, g in zip(vals[18:], ok[18:]) if g)
-            return tx, rx
-        except Exception:  # noqa: BLE001 - reported as unavailable
-            return None
-
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
@@ -405,7 +387,6 @@ def main():
             vk.set_option("clock_probe", 1)
             vk.read_clock_probe(local, clear=True)
         with ClockSampler(local) as clocks:
-            nvl0 = clocks.nvlink_kib() if world > 1 else None
             for i in range(args.steps):
                 if flush is not None:
                     flush.fill_(1.0)
@@ -414,7 +395,6 @@ def main():
                 ev[i][1].record(stream)
                 ev[i][1].synchronize()  # the reference driver synchronises every iteration
             barrier()
-            nvl1 = clocks.nvlink_kib() if world > 1 else None
         kernel_mhz = None
         if probe:
             kernel_mhz, _ = vk.read_clock_probe(local, clear=True)
@@ -536,12 +516,6 @@ def main():
                               if world > 1 else None),
             "e2e": e2e,
         }
-        if nvl0 is not None and nvl1 is not None:
-            tx, rx = (nvl1[0] - nvl0[0]) * 1024.0, (nvl1[1] - nvl0[1]) * 1024.0
-            line["nvlink_rank0"] = {
-                "tx_bytes_per_step": round(tx / args.steps), "rx_bytes_per_step": round(rx / args.steps),
-                "rx_gbs": round(rx / (total_ms * 1e-3) / 1e9, 1),
-                "source": "NVML NVLink data counters (TX/RX, all links) read around the timed steps"}
         if compute_ms is not None:
             line["compute_ms_per_step"] = round(compute_ms_max, 5)
             line["gather_ms_per_step"] = round(total_ms / args.steps - compute_ms_max, 5)

@@ -147,6 +147,7 @@ constexpr int kEpiPitch = 80;
 constexpr int kEpiBufBytes = 32 * 64;
 constexpr int kEpiWarpBytes = 2 * kEpiBufBytes;
 static_assert(kEpiWarpBytes >= 32 * kEpiPitch, "fallback staging fits the warp's area");
+static_assert(kEpiWarpBytes >= 32 * 128, "multicast staging (two chunks of 32 rows) fits the warp's area");
 
 template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
 struct TcCfg {
@@ -219,23 +220,36 @@ __device__ __forceinline__ void multimem_st_16(void* addr, const uint4& v)
                  : "memory");
 }
 
-// Fused all-gather through NVLS: one warp stores its staged 32 x 32 fp16 box (row r's 64 bytes at
-// `pitch`) once to the multicast view of C, 4 lanes per row so each instruction writes 64-byte runs
-// of 8 rows.  The host guarantees N and ldc are multiples of 8 and the view is 16-byte aligned, so
+// Fused all-gather through NVLS.  In this mode a warp's staging area holds 32 rows x 128 bytes: two
+// adjacent 32-column chunks of its rows (16-byte slot j of row r at j ^ (r & 7), so both the row
+// writes and the run reads below are bank-conflict free).  Pairs of chunks leave as 128-byte runs
+// (8 lanes per row, 4 rows per instruction): the NVSwitch replicates fewer, fuller packets than for
+// 64-byte runs.  The host guarantees N and ldc are multiples of 8 and the view is 16-byte aligned, so
 // every 16-byte segment with column < N is whole.
-__device__ __forceinline__ void store_box_multicast(const TcParams& p, const uint8_t* box, int pitch, int row0,
-                                                    int lane, int col)
+__device__ __forceinline__ void mc_store_runs(const TcParams& p, const uint8_t* stg, int row0, int lane, int col,
+                                              int width)
 {
-    const int seg = lane & 3;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int rr = (lane >> 2) + 8 * j;
+    const int lpr = width / 8;  // lanes per row: 8 (two chunks) or 4 (a lone chunk)
+    const int rpi = 32 / lpr;   // rows per store instruction
+    const int seg = lane % lpr;
+#pragma unroll 1
+    for (int i = 0; i < lpr; ++i) {
+        const int rr = lane / lpr + rpi * i;
         const int grow = row0 + rr;
         const int gcol = col + seg * 8;
-        if (grow >= p.M || gcol >= p.N) continue;
-        const uint4 v = *reinterpret_cast<const uint4*>(box + rr * pitch + seg * 16);
-        multimem_st_16(p.mc_c + static_cast<long long>(grow) * p.ldc + gcol, v);
+        if (grow < p.M && gcol < p.N) {
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((seg ^ (rr & 7)) * 16));
+            multimem_st_16(p.mc_c + static_cast<long long>(grow) * p.ldc + gcol, v);
+        }
     }
+    __syncwarp();
+}
+
+// Stores a staged chunk that is still waiting for its right-hand neighbour (mc_pend = its column).
+__device__ __forceinline__ void mc_flush(const TcParams& p, const uint8_t* stg, int row0, int lane, int& mc_pend)
+{
+    if (mc_pend >= 0) mc_store_runs(p, stg, row0, lane, mc_pend, 32);
+    mc_pend = -1;
 }
 
 // Fused all-gather: one warp copies its staged 32 x 32 fp16 box (rows row0.., columns col..; row r's
@@ -283,7 +297,7 @@ __device__ __forceinline__ void store_box_to_peers(const TcParams& p, const uint
 // default kernels' epilogue code stays exactly as it is without the exchange.
 template <int XG>
 __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap* tmap_c, uint8_t* stg, int row0,
-                                           int lane, int col, float (&f)[32], uint32_t& nbuf)
+                                           int lane, int col, float (&f)[32], uint32_t& nbuf, int& mc_pend)
 {
     const int row = row0 + lane;
     if (p.ep && row < p.M) {
@@ -310,6 +324,27 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
             for (int i = 0; i < 32; ++i)
                 if (col + i < p.N) d32[i] = f[i];
         }
+    }
+    if constexpr (XG == 2) {
+        // a chunk not adjacent to the pending one leaves alone first
+        if (mc_pend >= 0 && col != mc_pend + 32) mc_flush(p, stg, row0, lane, mc_pend);
+        const int h = mc_pend >= 0 ? 1 : 0;
+        uint4* srow = reinterpret_cast<uint4*>(stg + lane * 128);
+        const int sw = lane & 7;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            srow[(4 * h + j) ^ sw] = make_uint4(pack_half2(f[8 * j], f[8 * j + 1]), pack_half2(f[8 * j + 2], f[8 * j + 3]),
+                                                pack_half2(f[8 * j + 4], f[8 * j + 5]),
+                                                pack_half2(f[8 * j + 6], f[8 * j + 7]));
+        __syncwarp();
+        if (h == 1) {
+            mc_store_runs(p, stg, row0, lane, mc_pend, 64);
+            mc_pend = -1;
+        } else {
+            mc_pend = col;
+            if (col + 32 >= p.N) mc_flush(p, stg, row0, lane, mc_pend);  // no right-hand neighbour
+        }
+        return;
     }
     if (p.c_tma) {
         uint8_t* buf = stg + (nbuf & 1u) * kEpiBufBytes;
@@ -338,11 +373,6 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
         srow[j] = make_uint4(pack_half2(f[8 * j], f[8 * j + 1]), pack_half2(f[8 * j + 2], f[8 * j + 3]),
                              pack_half2(f[8 * j + 4], f[8 * j + 5]), pack_half2(f[8 * j + 6], f[8 * j + 7]));
     __syncwarp();
-    if constexpr (XG == 2) {
-        store_box_multicast(p, stg, kEpiPitch, row0, lane, col);
-        __syncwarp();
-        return;
-    }
     if constexpr (XG == 1) store_box_to_peers(p, stg, kEpiPitch, false, row0, lane, col);
     const int seg = lane & 3;
 #pragma unroll
@@ -606,6 +636,7 @@ __global__ void __launch_bounds__(192, 1)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         int it = 0;
         uint32_t nbuf = 0;       // 32-column chunks stored so far (staging buffer parity)
+        int mc_pend = -1;        // XG = 2: column of a staged chunk waiting for its neighbour
         for (int u = cluster_id; u < p.units; u += num_clusters, ++it) {
             const Unit w = unit_info(p, u);
             const int acc = it & 1;
@@ -721,7 +752,7 @@ __global__ void __launch_bounds__(192, 1)
                                     }
                                 }
                             }
-                            store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                            store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc_pend);
                         }
                     } else if (ok) {
                         __threadfence();
@@ -790,7 +821,7 @@ __global__ void __launch_bounds__(192, 1)
                                         }
                                     }
                                 }
-                                store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                                store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc_pend);
                             }
                             __syncwarp();
                         }
@@ -809,10 +840,11 @@ __global__ void __launch_bounds__(192, 1)
                     if (col0 + c < p.N) {
                         float f[32];
                         tmem_words_to_f32<ACC_F32>(r, f);
-                        store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf);
+                        store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc_pend);
                     }
                 }
             }
+            if constexpr (XG == 2) mc_flush(p, stg, row0, lane, mc_pend);
             tc_fence_before();
             __syncwarp();
             if (warp == 2 && lane == 0) {
