@@ -4,9 +4,11 @@ It exists for callers that cannot call cudaMalloc (work recorded during CUDA gra
 device memory owned by a pool or framework allocator, fixed memory budgets).  Its scratch is a
 fixed device array inside the library, so two calls in a row reuse the same array: the second
 call must not see stale arrival counters or partials from the first.  Each call is checked
-against the ordinary entry point vk_gemm on the same inputs, with the fp32-accumulate tolerances
-used throughout the GPU tests.  The file name makes pytest collect it last; it also passes alone
-in a fresh process.
+against the ordinary entry point vk_gemm on the same inputs and against the reference v0 (the
+oracle), with the tolerances used throughout the GPU tests, and the device's free memory must not
+move across calls made after the first one (which may load the library's device code), while an
+ordinary vk_gemm visibly allocates its scratch.  The file name makes pytest collect
+it last; it also passes alone in a fresh process.
 """
 import ctypes
 
@@ -64,6 +66,7 @@ def test_noalloc_matches_vk_gemm_on_two_calls_in_a_row(vk, shape, acc):
 
     r32 = ref32.cpu().numpy()
     r16 = ref.cpu().numpy()
+    g16, g32 = v0.v0_f16(A, B)  # the reference v0 (fp32 sgemm of the widened inputs)
     for C, C32 in outs:
         c32 = C32.cpu().numpy()
         c16 = C.cpu().numpy()
@@ -71,6 +74,48 @@ def test_noalloc_matches_vk_gemm_on_two_calls_in_a_row(vk, shape, acc):
         assert v0.rel_frobenius(c32, r32) <= FROB
         assert v0.max_elem_rel(c32, r32) <= ELEM
         assert v0.max_elem_rel(c16, r16) <= ELEM
+        if acc == "f32":  # fp32-accumulate tier against the oracle
+            assert v0.rel_frobenius(c32, g32) <= FROB
+            assert v0.max_elem_rel(c32, g32) <= ELEM
+            assert v0.max_elem_rel(c16, g16) <= ELEM
+        else:  # fp16-accumulate tier: relative Frobenius against the fp32 v0 result
+            assert v0.rel_frobenius(c16, g32) <= 5e-3
+
+
+def test_noalloc_allocates_nothing(vk):
+    """Free device memory stays put across no-allocation calls on a fresh stream whose plan needs
+    tail-split scratch, while vk_gemm (after vk_shutdown freed the library's scratch) allocates."""
+    m = n = k = 4096  # last wave cut into k-slices: the path that needs scratch
+    A, B = v0.make_inputs(m, n, k, 91)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    C = torch.empty((m, n), dtype=torch.float16, device="cuda")
+    C32 = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def call(entry, stream):
+        a = _args(vk, dA, dB, C, C32, "f32")
+        a.stream = stream.cuda_stream
+        vk.check(entry(ctypes.byref(a)))
+
+    call(vk.lib.vk_gemm_noalloc, s1)  # the first call may load the library's device code
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        call(vk.lib.vk_gemm_noalloc, s1)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"no-allocation calls changed free device memory by {free0 - free1} bytes"
+    g16, g32 = v0.v0_f16(A, B)
+    assert v0.rel_frobenius(C32.cpu().numpy(), g32) <= FROB
+    # control: after vk_shutdown has freed the library's scratch, the ordinary entry point allocates
+    # its tail-split scratch again, and the same measurement sees it
+    vk.check(vk.lib.vk_shutdown())
+    torch.cuda.synchronize()
+    free2, _ = torch.cuda.mem_get_info()
+    call(vk.lib.vk_gemm, s2)
+    torch.cuda.synchronize()
+    free3, _ = torch.cuda.mem_get_info()
+    assert free2 - free3 >= 16 << 20, "the measurement would not have seen an allocation"
 
 
 def test_noalloc_rejects_what_it_cannot_run(vk):
