@@ -147,9 +147,13 @@ constexpr int kEpiPitch = 80;
 constexpr int kEpiBufBytes = 32 * 64;
 constexpr int kEpiWarpBytes = 2 * kEpiBufBytes;
 static_assert(kEpiWarpBytes >= 32 * kEpiPitch, "fallback staging fits the warp's area");
-static_assert(kEpiWarpBytes >= 32 * 128, "multicast staging (two chunks of 32 rows) fits the warp's area");
+// Multicast epilogue (XG = 2): a warp stages up to kMcRunChunks adjacent 32-column chunks of its 32
+// rows (32 rows x 256 bytes) and sends them as runs of up to 256 bytes per row.
+constexpr int kMcRunChunks = 4;
+constexpr int kMcRowBytes = kMcRunChunks * 64;
+constexpr int kMcWarpBytes = 32 * kMcRowBytes;
 
-template <int CG, int BN, int STAGES, int KA, bool ACC_F32>
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32, int XG = 0>
 struct TcCfg {
     static constexpr int kBM = 128;              // rows per CTA (TMEM lanes)
     static constexpr int kBK = 64 * KA;          // k per stage: KA 128-byte swizzle spans of fp16
@@ -168,9 +172,10 @@ struct TcCfg {
     // The tail-split reduction stages other slices' partials in the (idle) pipeline buffers:
     // 48 KB per epilogue warp.
     static constexpr int kRedFloatsPerWarp = 12288;
+    static constexpr int kEpiWarp = XG == 2 ? kMcWarpBytes : kEpiWarpBytes;  // staging bytes per epilogue warp
     static constexpr int kSmemBytes =
         1024 /*alignment slack*/ + STAGES * kStageBytes + kNumBars * 8 + 32 + 1024 /*staging alignment*/ +
-        4 * kEpiWarpBytes;
+        4 * kEpiWarp;
     static constexpr int kThreads = 192;
     static_assert(CG == 1 || CG == 2, "cta group");
     static_assert(KA == 1 || KA == 2, "k spans per stage");
@@ -220,36 +225,37 @@ __device__ __forceinline__ void multimem_st_16(void* addr, const uint4& v)
                  : "memory");
 }
 
-// Fused all-gather through NVLS.  In this mode a warp's staging area holds 32 rows x 128 bytes: two
-// adjacent 32-column chunks of its rows (16-byte slot j of row r at j ^ (r & 7), so both the row
-// writes and the run reads below are bank-conflict free).  Pairs of chunks leave as 128-byte runs
-// (8 lanes per row, 4 rows per instruction): the NVSwitch replicates fewer, fuller packets than for
-// 64-byte runs.  The host guarantees N and ldc are multiples of 8 and the view is 16-byte aligned, so
-// every 16-byte segment with column < N is whole.
-__device__ __forceinline__ void mc_store_runs(const TcParams& p, const uint8_t* stg, int row0, int lane, int col,
-                                              int width)
-{
-    const int lpr = width / 8;  // lanes per row: 8 (two chunks) or 4 (a lone chunk)
-    const int rpi = 32 / lpr;   // rows per store instruction
-    const int seg = lane % lpr;
-#pragma unroll 1
-    for (int i = 0; i < lpr; ++i) {
-        const int rr = lane / lpr + rpi * i;
-        const int grow = row0 + rr;
-        const int gcol = col + seg * 8;
-        if (grow < p.M && gcol < p.N) {
-            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((seg ^ (rr & 7)) * 16));
-            multimem_st_16(p.mc_c + static_cast<long long>(grow) * p.ldc + gcol, v);
-        }
-    }
-    __syncwarp();
-}
+// Fused all-gather through NVLS.  In this mode a warp's staging area holds 32 rows x 256 bytes: up
+// to four adjacent 32-column chunks of its rows (16-byte slot j of row r at j ^ (r & 7), so the row
+// writes and the run reads below are bank-conflict free).  The staged chunks leave together as runs of
+// up to 256 bytes per row (16 lanes per row, 2 rows per store instruction): the NVSwitch replicates
+// fewer, fuller packets than for 64-byte runs (measured on 8 GPUs: 64-byte runs 1.33 ms per 16384^3
+// step, 128-byte runs 1.09 ms).  The host guarantees N and ldc are multiples of 8 and the view is
+// 16-byte aligned, so every 16-byte segment with column < N is whole.
+struct McRun {
+    int col = -1;  // first column of the staged run (-1: nothing staged)
+    int n = 0;     // 32-column chunks staged
+};
 
-// Stores a staged chunk that is still waiting for its right-hand neighbour (mc_pend = its column).
-__device__ __forceinline__ void mc_flush(const TcParams& p, const uint8_t* stg, int row0, int lane, int& mc_pend)
+__device__ __forceinline__ void mc_flush(const TcParams& p, const uint8_t* stg, int row0, int lane, McRun& run)
 {
-    if (mc_pend >= 0) mc_store_runs(p, stg, row0, lane, mc_pend, 32);
-    mc_pend = -1;
+    if (run.n > 0) {
+        const int spr = run.n * 4;  // 16-byte segments per row
+#pragma unroll 1
+        for (int idx = lane; idx < 32 * spr; idx += 32) {
+            const int rr = idx / spr;
+            const int seg = idx - rr * spr;
+            const int grow = row0 + rr;
+            const int gcol = run.col + seg * 8;
+            if (grow < p.M && gcol < p.N) {
+                const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * kMcRowBytes + ((seg ^ (rr & 7)) * 16));
+                multimem_st_16(p.mc_c + static_cast<long long>(grow) * p.ldc + gcol, v);
+            }
+        }
+        __syncwarp();
+    }
+    run.col = -1;
+    run.n = 0;
 }
 
 // Fused all-gather: one warp copies its staged 32 x 32 fp16 box (rows row0.., columns col..; row r's
@@ -297,7 +303,7 @@ __device__ __forceinline__ void store_box_to_peers(const TcParams& p, const uint
 // default kernels' epilogue code stays exactly as it is without the exchange.
 template <int XG>
 __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap* tmap_c, uint8_t* stg, int row0,
-                                           int lane, int col, float (&f)[32], uint32_t& nbuf, int& mc_pend)
+                                           int lane, int col, float (&f)[32], uint32_t& nbuf, McRun& mc)
 {
     const int row = row0 + lane;
     if (p.ep && row < p.M) {
@@ -326,24 +332,20 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
         }
     }
     if constexpr (XG == 2) {
-        // a chunk not adjacent to the pending one leaves alone first
-        if (mc_pend >= 0 && col != mc_pend + 32) mc_flush(p, stg, row0, lane, mc_pend);
-        const int h = mc_pend >= 0 ? 1 : 0;
-        uint4* srow = reinterpret_cast<uint4*>(stg + lane * 128);
+        // a chunk that does not continue the staged run sends the run first
+        if (mc.n > 0 && col != mc.col + 32 * mc.n) mc_flush(p, stg, row0, lane, mc);
+        if (mc.n == 0) mc.col = col;
+        uint4* srow = reinterpret_cast<uint4*>(stg + lane * kMcRowBytes);
         const int sw = lane & 7;
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-            srow[(4 * h + j) ^ sw] = make_uint4(pack_half2(f[8 * j], f[8 * j + 1]), pack_half2(f[8 * j + 2], f[8 * j + 3]),
-                                                pack_half2(f[8 * j + 4], f[8 * j + 5]),
-                                                pack_half2(f[8 * j + 6], f[8 * j + 7]));
+            srow[(4 * mc.n + j) ^ sw] = make_uint4(pack_half2(f[8 * j], f[8 * j + 1]),
+                                                   pack_half2(f[8 * j + 2], f[8 * j + 3]),
+                                                   pack_half2(f[8 * j + 4], f[8 * j + 5]),
+                                                   pack_half2(f[8 * j + 6], f[8 * j + 7]));
         __syncwarp();
-        if (h == 1) {
-            mc_store_runs(p, stg, row0, lane, mc_pend, 64);
-            mc_pend = -1;
-        } else {
-            mc_pend = col;
-            if (col + 32 >= p.N) mc_flush(p, stg, row0, lane, mc_pend);  // no right-hand neighbour
-        }
+        ++mc.n;
+        if (mc.n == kMcRunChunks || col + 32 >= p.N) mc_flush(p, stg, row0, lane, mc);  // full, or row end
         return;
     }
     if (p.c_tma) {
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(192, 1)
                    const __grid_constant__ CUtensorMap tmap_c, const TcParams p)
 {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-    using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32>;
+    using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32, XG>;
     constexpr int BM = Cfg::kBM;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -636,7 +638,7 @@ __global__ void __launch_bounds__(192, 1)
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         int it = 0;
         uint32_t nbuf = 0;       // 32-column chunks stored so far (staging buffer parity)
-        int mc_pend = -1;        // XG = 2: column of a staged chunk waiting for its neighbour
+        McRun mc;                // XG = 2: chunks staged for the next multicast run
         for (int u = cluster_id; u < p.units; u += num_clusters, ++it) {
             const Unit w = unit_info(p, u);
             const int acc = it & 1;
@@ -648,7 +650,7 @@ __global__ void __launch_bounds__(192, 1)
             int tm, tn;
             tile_coords(w.tile, p.tiles_m, p.tiles_n, p.raster_group, tm, tn);
             const int row0 = tm * (BM * CG) + static_cast<int>(rank) * BM + q * 32;  // this warp's rows
-            uint8_t* stg = epi_stage + q * kEpiWarpBytes;
+            uint8_t* stg = epi_stage + q * Cfg::kEpiWarp;
             const int col0 = tn * BN + (w.half > 0 ? BN / 2 : 0);
             const int bn_eff = w.half >= 0 ? BN / 2 : BN;  // columns of this unit
             const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
@@ -752,7 +754,7 @@ __global__ void __launch_bounds__(192, 1)
                                     }
                                 }
                             }
-                            store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc_pend);
+                            store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc);
                         }
                     } else if (ok) {
                         __threadfence();
@@ -821,7 +823,7 @@ __global__ void __launch_bounds__(192, 1)
                                         }
                                     }
                                 }
-                                store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc_pend);
+                                store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc);
                             }
                             __syncwarp();
                         }
@@ -840,11 +842,11 @@ __global__ void __launch_bounds__(192, 1)
                     if (col0 + c < p.N) {
                         float f[32];
                         tmem_words_to_f32<ACC_F32>(r, f);
-                        store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc_pend);
+                        store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc);
                     }
                 }
             }
-            if constexpr (XG == 2) mc_flush(p, stg, row0, lane, mc_pend);
+            if constexpr (XG == 2) mc_flush(p, stg, row0, lane, mc);
             tc_fence_before();
             __syncwarp();
             if (warp == 2 && lane == 0) {

@@ -469,7 +469,7 @@ struct Problem {
 template <int CG, int BN, int STAGES, int KA, bool ACC_F32, int XG = 0>
 static int launch_tc(DeviceState& st, int dev, const Problem& pb, const FixedScratch* fixed)
 {
-    using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32>;
+    using Cfg = TcCfg<CG, BN, STAGES, KA, ACC_F32, XG>;
     auto fn = tc_gemm_kernel<CG, BN, STAGES, KA, ACC_F32, XG>;
     int max_units = 0;
     int rc = kernel_slot(st, fn, Cfg::kSmemBytes, Cfg::kThreads, CG, &max_units);
