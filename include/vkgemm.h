@@ -264,6 +264,11 @@ int vk_set_wait_timeout_ns(uint64_t ns);
  *                     leftover tiles can be cut into 2..4 k-slices, those slices run before the
  *                     whole tiles (their partial sums are reduced while the tensor pipes work on
  *                     whole tiles); 0 = leftover tiles run last, policy of "tail_nsplit"
+ *   "k_chains"        0 (default) = off; 1 = when k > 8192, the default pair kernel runs each output tile's
+ *                     k range as two accumulation chains (its two TMEM accumulators) summed in fp32 by the
+ *                     epilogue: the tensor cores' truncating fp32 accumulation drifts about half as far
+ *                     (16384^3: per-element error 3.7e-3 -> 1.9e-3), at the cost of the epilogue /
+ *                     main-loop overlap (up to 19 % slower on short-M shapes); 2 = always (k > 128)
  *   "tma_store"       1 (default) = the tensor-core kernels write fp16 C with TMA tile stores when C
  *                     is 16-byte aligned with a pitch that is a multiple of 8 elements; 0 = always
  *                     per-lane coalesced stores (the path taken for any other C)

@@ -290,6 +290,26 @@ __device__ __forceinline__ void store_box_to_peers(const TcParams& p, const uint
     }
 }
 
+// One 32-column chunk of this warp's accumulator rows as fp32 values: the TMEM words at `taddr`, plus,
+// with two accumulation chains (CH), the second chain's words at `taddr2`, added in fp32 (the second
+// load reuses the first one's registers).
+template <bool ACC_F32, bool CH>
+__device__ __forceinline__ void acc_chunk(uint32_t taddr, uint32_t taddr2, float (&f)[32])
+{
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr, r);
+    tmem_ld_wait();
+    tmem_words_to_f32<ACC_F32>(r, f);
+    if constexpr (CH) {
+        tmem_ld_32x32b_x32(taddr2, r);
+        tmem_ld_wait();
+        float g[32];
+        tmem_words_to_f32<ACC_F32>(r, g);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) f[i] += g[i];
+    }
+}
+
 // One warp writes its 32 rows x 32 columns of C (this lane's row = row0 + lane, values f for
 // columns col .. col+31): the fused epilogue and the fp32 copy are applied per row, then the fp16
 // results go through the warp's staging buffer.  With a C tensor map (c_tma) lane 0 stores the
@@ -398,7 +418,13 @@ __device__ __forceinline__ void store_rows(const TcParams& p, const CUtensorMap*
     __syncwarp();
 }
 
-template <int CG, int BN, int STAGES, int KA, bool ACC_F32, int XG = 0>
+// CH (two accumulation chains): each unit's k range runs as two independent chains, the first half
+// into TMEM accumulator 0 and the second into accumulator 1, summed in fp32 by the epilogue.  The MMA's
+// fp32 accumulation truncates the aligned addends, so its error grows with the chain length; two
+// half-length chains halve it (K = 16384: per-element error of the fp16 result 3.7e-3 -> see the
+// parity tests).  Both accumulators serve one unit, so the epilogue no longer overlaps the next
+// unit's main loop; units need >= 2 k-blocks (slices have >= 4).
+template <int CG, int BN, int STAGES, int KA, bool ACC_F32, int XG = 0, bool CH = false>
 __global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_c, const TcParams p)
@@ -573,11 +599,15 @@ __global__ void __launch_bounds__(192, 1)
             bool ok = true;
             for (int u = cluster_id; ok && u < p.units; u += num_clusters, ++it) {
                 const Unit w = unit_info(p, u);
-                const int acc = it & 1;
-                const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
+                // alternate accumulators between units, or (chains) both for every unit, signalled on
+                // the barriers of accumulator 0
+                const int acc = CH ? 0 : (it & 1);
+                const uint32_t acc_phase = CH ? (static_cast<uint32_t>(it) & 1u) : (static_cast<uint32_t>(it >> 1) & 1u);
                 if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, kErrWaitMma, 100 + acc)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                // first k-block of the second chain (w.kb1: no second chain); units have >= 2 k-blocks
+                const int kmid = CH ? (w.kb0 + w.kb1 + 1) / 2 : w.kb1;
                 const uint32_t idesc = w.half >= 0 ? kIdescHalf : kIdesc;
                 for (int kb = w.kb0; kb < w.kb1; ++kb) {
                     if (!mbar_wait(full_bar(stage), phase, p.timeout_ns, kErrWaitMma, stage)) {
@@ -600,7 +630,8 @@ __global__ void __launch_bounds__(192, 1)
                         const uint64_t b_desc =
                             B_K ? smem_desc_sw128(b_addr + (kk >> 2) * Cfg::kBKBox + (kk & 3) * 32, 16, 1024)
                                 : smem_desc_sw128(b_addr + kk * 16 * 128, kMnLbo, 1024);
-                        umma_f16<CG>(d_tmem, a_desc, b_desc, idesc, (kb != w.kb0 || kk != 0) ? 1u : 0u);
+                        const uint32_t d = kb >= kmid ? tmem_base + static_cast<uint32_t>(BN) : d_tmem;
+                        umma_f16<CG>(d, a_desc, b_desc, idesc, ((kb != w.kb0 && kb != kmid) || kk != 0) ? 1u : 0u);
                     }
                     const uint32_t eb = empty_bar(stage);
                     umma_commit<CG>(eb);
@@ -641,8 +672,8 @@ __global__ void __launch_bounds__(192, 1)
         McRun mc;                // XG = 2: chunks staged for the next multicast run
         for (int u = cluster_id; u < p.units; u += num_clusters, ++it) {
             const Unit w = unit_info(p, u);
-            const int acc = it & 1;
-            const uint32_t acc_phase = static_cast<uint32_t>(it >> 1) & 1u;
+            const int acc = CH ? 0 : (it & 1);
+            const uint32_t acc_phase = CH ? (static_cast<uint32_t>(it) & 1u) : (static_cast<uint32_t>(it >> 1) & 1u);
             if (!mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns, kErrWaitEpilogue, acc)) break;
             if (it == 0 && warp == 2 && lane == 0) trace_at(p.trace, 5);
             if (p.trace && warp == 2 && lane == 0 && blockIdx.x < 256) g_trace_cta[blockIdx.x][6] = globaltimer_ns();
@@ -654,6 +685,7 @@ __global__ void __launch_bounds__(192, 1)
             const int col0 = tn * BN + (w.half > 0 ? BN / 2 : 0);
             const int bn_eff = w.half >= 0 ? BN / 2 : BN;  // columns of this unit
             const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+            const uint32_t tbase2 = tmem_base + static_cast<uint32_t>(BN) + (static_cast<uint32_t>(q * 32) << 16);
             if (w.slice >= 0) {
                 // Tail slice.  Arrivals are counted first: every slice but the last to arrive publishes
                 // its fp32 partial (lane-major float4 runs: each warp store is one contiguous 512-byte
@@ -670,11 +702,8 @@ __global__ void __launch_bounds__(192, 1)
                     float* mine = p.ws + (static_cast<size_t>(ti * p.split + w.slice) * CG + rank) * kRegion + warp_off;
 #pragma unroll 1
                     for (int c = 0; c < BN; c += 32) {
-                        uint32_t r[32];
-                        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
-                        tmem_ld_wait();
                         float f[32];
-                        tmem_words_to_f32<ACC_F32>(r, f);
+                        acc_chunk<ACC_F32, CH>(tbase + static_cast<uint32_t>(c), tbase2 + static_cast<uint32_t>(c), f);
                         float4* dst = reinterpret_cast<float4*>(mine + c * 32);
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
@@ -717,6 +746,14 @@ __global__ void __launch_bounds__(192, 1)
                             tmem_ld_wait();
                             float own[32];
                             tmem_words_to_f32<ACC_F32>(r, own);
+                            if constexpr (CH) {
+                                tmem_ld_32x32b_x32(tbase2 + static_cast<uint32_t>(c), r);
+                                tmem_ld_wait();
+                                float own2[32];
+                                tmem_words_to_f32<ACC_F32>(r, own2);
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) own[i] += own2[i];
+                            }
                             // f = ((p_0 + p_1) + p_2) + ... in slice order, p_own taken from TMEM
                             float f[32];
 #pragma unroll 1
@@ -784,11 +821,9 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
                             for (int c = c0; c < c0 + cr; c += 32) {
                                 if (col0 + c >= p.N) break;
-                                uint32_t r[32];
-                                tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
-                                tmem_ld_wait();
                                 float own[32];
-                                tmem_words_to_f32<ACC_F32>(r, own);
+                                acc_chunk<ACC_F32, CH>(tbase + static_cast<uint32_t>(c), tbase2 + static_cast<uint32_t>(c),
+                                                       own);
                                 // f = ((p_0 + p_1) + p_2) + ... in slice order, p_own taken from TMEM
                                 float f[32];
                                 int j = 0;
@@ -836,12 +871,9 @@ __global__ void __launch_bounds__(192, 1)
             } else {
 #pragma unroll 1
                 for (int c = 0; c < bn_eff; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), r);
-                    tmem_ld_wait();
+                    float f[32];
+                    acc_chunk<ACC_F32, CH>(tbase + static_cast<uint32_t>(c), tbase2 + static_cast<uint32_t>(c), f);
                     if (col0 + c < p.N) {
-                        float f[32];
-                        tmem_words_to_f32<ACC_F32>(r, f);
                         store_rows<XG>(p, &tmap_c, stg, row0, lane, col0 + c, f, nbuf, mc);
                     }
                 }
