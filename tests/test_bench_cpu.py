@@ -34,3 +34,28 @@ def test_bench_rejects_too_few_warmups():
     r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--warmup", "2"],
                        capture_output=True, text=True, timeout=120, cwd=ROOT)
     assert r.returncode != 0 and "warmup" in r.stderr
+
+
+def test_output_check_catches_a_planted_mistake():
+    """bench.check_rows (the bench's own check of its timed output against golden rows) passes the
+    golden rows themselves and fails a planted error in each tier."""
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import bench
+    rows, gold = bench.golden("cfg1_4096_seed1")
+    assert bench.check_rows(gold.copy(), gold, "f32", "f16")["ok"]
+    bad = gold.copy()
+    bad[3, 17] = np.float16(float(gold[3, 17]) * 1.01 + 0.5)
+    assert not bench.check_rows(bad, gold, "f32", "f16")["ok"]
+    nan = gold.copy()
+    nan[0, 0] = np.float16("nan")
+    assert not bench.check_rows(nan, gold, "f32", "f16")["ok"]
+    rows2, gold2 = bench.golden("cfg2_4096_seed2")
+    assert bench.check_rows(gold2.copy(), gold2, "f16", "f16")["ok"]
+    assert not bench.check_rows(gold2 * np.float16(1.01), gold2, "f16", "f16")["ok"]
+    rows3, gold3 = bench.golden("cfg3_sgemm_4096_seed3")
+    assert bench.check_rows(gold3.copy(), gold3, "f32", "f32")["ok"]
+    assert not bench.check_rows(gold3 * np.float32(1.0001), gold3, "f32", "f32")["ok"]
+    rows4, gold4 = bench.golden("cfg4a_16384_seed4")
+    assert bench.check_rows(gold4.copy(), gold4, "f32", "f16")["ok"]
+    assert not bench.check_rows(gold4[:, ::-1].copy(), gold4, "f32", "f16")["ok"]
