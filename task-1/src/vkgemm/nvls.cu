@@ -484,6 +484,22 @@ extern "C" int vk_mc_attach(vk_mc_team* t, void** local_ptr, void** mc_ptr, size
         t->mem.push_back(mem);
         t->uc.push_back(uc);
         rc = map_multicast(t);
+        if (rc != VK_OK) {
+            // undo this member's mapping and binding at once, so that it never leaves with memory bound;
+            // the object itself is released by vk_mc_detach
+            if (t->mc_va != 0) {
+                g_drv.MemUnmap(t->mc_va, t->size);
+                g_drv.MemAddressFree(t->mc_va, t->size);
+                t->mc_va = 0;
+            }
+            g_drv.MemUnmap(uc, t->size);
+            g_drv.MemAddressFree(uc, t->size);
+            CUdevice cd;
+            if (g_drv.DeviceGet(&cd, dev) == CUDA_SUCCESS) g_drv.MulticastUnbind(t->mc, cd, 0, t->size);
+            g_drv.MemRelease(mem);
+            t->mem.clear();
+            t->uc.clear();
+        }
     }
     if (rc != VK_OK) return rc;
     t->attached = true;

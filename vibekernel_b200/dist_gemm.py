@@ -165,7 +165,11 @@ class McRowGather:
                 lib.vk_mc_detach(team)
             raise RuntimeError("multicast buffer setup failed: " + "; ".join(failed))
         local, mc, size = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_size_t()
-        check(lib.vk_mc_attach(team, ctypes.byref(local), ctypes.byref(mc), ctypes.byref(size)))
+        rc = lib.vk_mc_attach(team, ctypes.byref(local), ctypes.byref(mc), ctypes.byref(size))
+        if rc != 0:
+            msg = _err_text(rc)
+            lib.vk_mc_detach(team)  # releases this member's share; nothing of it stays bound
+            raise RuntimeError(f"multicast buffer attach failed on rank {rank}: {msg}")
         dist.barrier(group=group)  # every member bound before anyone stores through the multicast view
         self._team = team
         self.mc = int(mc.value)
