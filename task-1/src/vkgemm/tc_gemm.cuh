@@ -38,6 +38,10 @@
 // sums all slices in slice order (its own from TMEM, the others from the workspace) -- the same
 // order whoever arrives last, so results are bitwise reproducible -- writes C, and resets the
 // counters.  Alternatively (nsplit) each tail tile is cut into two column halves.
+//
+// Kernel instances beyond the default: XG = 1 / 2 add the all-gather of C to the epilogue (stores
+// into every peer's C, or once into the NVLS multicast view of C, which replaces the local store);
+// CH runs each unit's k range as two accumulation chains in the two accumulators (see the kernel).
 #pragma once
 
 #include <cuda_fp16.h>
