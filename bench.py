@@ -339,7 +339,16 @@ def main():
     gather_on = mode != "none"
     mc_gather = peer_gather = None
     if mode == "nvls":
-        mc_gather = dist_gemm.McRowGather(m_total, n, off, rank, dtype=tdt)
+        try:
+            mc_gather = dist_gemm.McRowGather(m_total, n, off, rank, dtype=tdt)
+        except dist_gemm.McSetupRefused as e:
+            # a refused multicast object is reported to every rank at the same point, so all fall back
+            if args.allgather != "auto":
+                raise
+            if rank == 0:
+                print(f"warning: NVLS multicast unavailable ({e}); gathering C with NCCL", file=sys.stderr)
+            mode = "nccl"
+    if mc_gather is not None:
         C_full = mc_gather.C_full
     else:
         C_full = torch.empty((m_total, n), dtype=tdt, device=dev) if gather_on else None

@@ -122,6 +122,10 @@ class PeerRowGather:
         self.peers = {}
 
 
+class McSetupRefused(RuntimeError):
+    """The multicast object could not be created or imported; raised on every rank together."""
+
+
 class McRowGather:
     """All-gather of C row blocks fused into the GEMM through an NVLS multicast buffer (one process
     per GPU, NVSwitch systems: ``vibekernel_b200.mc_supported``).
@@ -163,7 +167,7 @@ class McRowGather:
         if failed:
             if team.value:
                 lib.vk_mc_detach(team)
-            raise RuntimeError("multicast buffer setup failed: " + "; ".join(failed))
+            raise McSetupRefused("multicast buffer setup failed: " + "; ".join(failed))
         local, mc, size = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_size_t()
         rc = lib.vk_mc_attach(team, ctypes.byref(local), ctypes.byref(mc), ctypes.byref(size))
         if rc != 0:
