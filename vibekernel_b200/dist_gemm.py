@@ -142,7 +142,7 @@ class McRowGather:
         import torch
         import torch.distributed as dist
 
-        from . import _view, check, lib
+        from . import _view, lib
         dtype = dtype or torch.float16
         self.off, self.rank, self.group = list(off), rank, group
         world = len(off) - 1
