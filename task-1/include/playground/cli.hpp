@@ -69,7 +69,9 @@ public:
                "      --seed arg       Input seed (default: std::random_device)\n"
                "      --dist arg       normal (default) or uniform\n"
                "      --lo arg, --hi arg   uniform range (default -1, 1)\n"
-               "      --json arg       also write the result as one JSON line to this file\n";
+               "      --json arg       also write the result as one JSON line to this file\n"
+               "      --gpus arg       split the rows over GPUs 0..arg-1 (vk_gemm_sharded; GPU versions)\n"
+               "      --allgather arg  none | nccl (default) | pipelined | fused | nvls: all-gather of C\n";
     }
 
 private:

@@ -7,8 +7,15 @@
 // Additive lines follow it: the rel-Frobenius and per-element errors of an fp32 copy of C (from one
 // extra verification launch of the same kernel), the SM clock the kernels ran at (in-kernel probe),
 // the seed, and the fraction of the 2.25 PFLOP/s dense fp16 figure.
+//
+// Additive multi-GPU mode (--gpus P, GPU versions only): the same problem split into P row blocks of A
+// and C over devices 0..P-1 with B copied to each, run through vk_gemm_sharded with the all-gather of C
+// chosen by --allgather (none | nccl | pipelined | fused | nvls); the timed loop and the result line are
+// those of one GPU, the time of a call is its slowest GPU's compute plus the gather.
 #include <chrono>
+#include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <exception>
 #include <string>
 #include <vector>
@@ -159,6 +166,109 @@ void test(std::uint32_t m, std::uint32_t n, std::uint32_t k, std::uint32_t nWarm
         }
     }
 }
+// vk_gemm_sharded's arguments for this build's version: dtype, accumulate tier and kernel.
+void shardKind(vk_shard_args& a)
+{
+#if defined(TEST_FLOAT16)
+    a.dtype = VK_DTYPE_F16;
+    switch (params::MatmulVersion) {
+        case 2: a.algo = VK_ALGO_TC_2SM; a.acc = VK_ACC_F16; break;
+        case 3: a.algo = VK_ALGO_TC_1SM; a.acc = VK_ACC_F32; break;
+        case 4: a.algo = VK_ALGO_SIMT; a.acc = VK_ACC_F32; break;
+        default: a.algo = VK_ALGO_TC_2SM; a.acc = VK_ACC_F32; break;
+    }
+#else
+    a.dtype = VK_DTYPE_F32;
+    a.acc = VK_ACC_F32;
+    a.algo = VK_ALGO_FFMA;
+#endif
+}
+
+void testSharded(std::uint32_t m, std::uint32_t n, std::uint32_t k, std::uint32_t nWarmupRound, std::uint32_t nTestRound,
+                 const DataOptions& opt, int gpus, const std::string& mode)
+{
+    int count = 0;
+    PLAYGROUND_CHECK(cudaGetDeviceCount(&count) == cudaSuccess);
+    if (gpus < 1 || gpus > count)
+        throw std::invalid_argument("--gpus " + std::to_string(gpus) + ": " + std::to_string(count) + " GPU(s) visible");
+    const int gather = mode == "none" ? 0 : mode == "nccl" ? 1 : mode == "pipelined" ? 2 : mode == "fused" ? 3
+                     : mode == "nvls" ? 4 : -1;
+    if (gather < 0) throw std::invalid_argument("--allgather must be none, nccl, pipelined, fused or nvls");
+    TestData testData(m, n, k, opt);
+    std::printf("[Playground] Start Testing for GEMM Version %u with DType %s on %d GPU(s), all-gather %s ...\n",
+                static_cast<unsigned>(params::MatmulVersion), params::DataTypeName.data(), gpus, mode.c_str());
+    const size_t es = sizeof(params::DataType);
+    std::vector<int32_t> devs(gpus);
+    std::vector<int64_t> off(gpus + 1);
+    for (int r = 0; r <= gpus; ++r) off[r] = static_cast<int64_t>(m) * r / gpus;
+    std::vector<void*> A(gpus), B(gpus), C(gpus);
+    void* mc = nullptr;
+    for (int r = 0; r < gpus; ++r) devs[r] = r;
+    if (gather == 4) vkCheck(vk_mc_alloc(gpus, devs.data(), static_cast<size_t>(m) * n * es, C.data(), &mc), "vk_mc_alloc");
+    for (int r = 0; r < gpus; ++r) {
+        PLAYGROUND_CHECK(cudaSetDevice(r) == cudaSuccess);
+        const size_t rows = static_cast<size_t>(off[r + 1] - off[r]);
+        PLAYGROUND_CHECK(cudaMalloc(&A[r], std::max<size_t>(rows * k * es, 16)) == cudaSuccess);
+        PLAYGROUND_CHECK(cudaMalloc(&B[r], static_cast<size_t>(k) * n * es) == cudaSuccess);
+        if (gather != 4) PLAYGROUND_CHECK(cudaMalloc(&C[r], static_cast<size_t>(m) * n * es) == cudaSuccess);
+        PLAYGROUND_CHECK(cudaMemcpy(A[r], testData.get_mutable_A_ptr() + off[r] * k, rows * k * es,
+                                    cudaMemcpyHostToDevice) == cudaSuccess);
+        PLAYGROUND_CHECK(cudaMemcpy(B[r], testData.get_mutable_B_ptr(), static_cast<size_t>(k) * n * es,
+                                    cudaMemcpyHostToDevice) == cudaSuccess);
+    }
+    vk_shard_args a{};
+    a.ngpu = gpus;
+    a.devices = devs.data();
+    a.A = A.data();
+    a.B = B.data();
+    a.C = C.data();
+    a.m = m;
+    a.n = n;
+    a.k = k;
+    shardKind(a);
+    a.allgather_c = gather;
+    float times[2] = {0.f, 0.f};
+    a.times_ms = times;
+    for (std::uint32_t i = 0; i < nWarmupRound; ++i) vkCheck(vk_gemm_sharded(&a), "vk_gemm_sharded");
+    float32_t totalMilliSecs = 0.0f;
+    for (std::uint32_t i = 0; i < nTestRound; ++i) {  // each call returns after every GPU (and the gather)
+        vkCheck(vk_gemm_sharded(&a), "vk_gemm_sharded");
+        totalMilliSecs += times[0] + times[1];
+    }
+    // C on the host: every GPU's own rows (without a gather), or GPU 0's full C (with one), and every
+    // other GPU's full C must then be bitwise the same
+    params::DataType* hC = testData.get_mutable_C_ptr();
+    bool same = true;
+    for (int r = 0; r < gpus; ++r) {
+        PLAYGROUND_CHECK(cudaSetDevice(r) == cudaSuccess);
+        if (gather == 0 || r == 0) {
+            const size_t r0 = gather == 0 ? static_cast<size_t>(off[r]) : 0;
+            const size_t rows = gather == 0 ? static_cast<size_t>(off[r + 1] - off[r]) : m;
+            PLAYGROUND_CHECK(cudaMemcpy(hC + r0 * n, static_cast<char*>(C[r]) + r0 * n * es, rows * n * es,
+                                        cudaMemcpyDeviceToHost) == cudaSuccess);
+        } else {
+            std::vector<params::DataType> other(static_cast<size_t>(m) * n);
+            PLAYGROUND_CHECK(cudaMemcpy(other.data(), C[r], other.size() * es, cudaMemcpyDeviceToHost) == cudaSuccess);
+            same = same && std::memcmp(other.data(), hC, other.size() * es) == 0;
+        }
+    }
+    for (int r = 0; r < gpus; ++r) {
+        cudaSetDevice(r);
+        cudaFree(A[r]);
+        cudaFree(B[r]);
+        if (gather != 4) cudaFree(C[r]);
+    }
+    if (mc != nullptr) vkCheck(vk_mc_free(mc), "vk_mc_free");
+    cudaSetDevice(0);
+    std::printf("[Playground] Calculating Finished\n");
+    const float32_t avgErr = testData.calculateAvgErr();
+    const float32_t msecPerMatrixMul = totalMilliSecs / static_cast<float32_t>(nTestRound);
+    const float64_t tflops = (2.0 * m * n * k * 1.0e-12) / (msecPerMatrixMul / 1000.0);
+    std::printf("[Playground] Result >>> TFLOPS: %g; Average Error: %g\n", tflops, avgErr);
+    std::printf("[Playground] Sharded >>> GPUs: %d; AllGather: %s; AllGpusEqual: %d; ComputeMs: %.4f; GatherMs: %.4f\n",
+                gpus, mode.c_str(), same ? 1 : 0, times[0], times[1]);
+    PLAYGROUND_CHECK(same);
+}
 }  // namespace
 
 int main(int argc, const char* argv[])
@@ -175,6 +285,12 @@ int main(int argc, const char* argv[])
         opt.lo = cli.f64("lo", -1.0);
         opt.hi = cli.f64("hi", 1.0);
         if (opt.dist != "normal" && opt.dist != "uniform") throw std::invalid_argument("--dist must be normal or uniform");
+        if (cli.has("gpus")) {
+            if constexpr (USING_CPU_MATMUL) throw std::invalid_argument("--gpus needs a GPU version (v >= 1)");
+            testSharded(cli.u32("m", 4096), cli.u32("n", 4096), cli.u32("k", 4096), cli.u32("w", 10),
+                        cli.u32("t", 100), opt, static_cast<int>(cli.u32("gpus", 1)), cli.str("allgather", "nccl"));
+            return 0;
+        }
         test(cli.u32("m", 4096), cli.u32("n", 4096), cli.u32("k", 4096), cli.u32("w", 10), cli.u32("t", 100), opt,
              cli.str("json", ""));
     } catch (const std::exception& e) {

@@ -37,6 +37,33 @@ def test_v0_cpu_paths_and_result_line(built):
         assert "Start Testing for GEMM Version 0" in r.stdout
 
 
+SHARDED = re.compile(r"Sharded >>> GPUs: (\d+); AllGather: (\w+); AllGpusEqual: (\d)")
+
+
+def test_gpus_option_needs_a_gpu_version(built):
+    r = _run("task1_float16_v0", "--gpus", "2", "-m", "64", "-n", "64", "-k", "64")
+    assert r.returncode == 2 and "GPU version" in r.stderr
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gpus,mode", [(1, "none"), (1, "nccl"), (2, "none"), (2, "nccl"), (2, "pipelined"),
+                                       (2, "fused"), (2, "nvls")])
+def test_sharded_driver(built, gpus, mode):
+    """--gpus: the driver's row-sharded mode through vk_gemm_sharded, error check against v0."""
+    import torch
+    if torch.cuda.device_count() < gpus:
+        pytest.skip(f"needs {gpus} GPUs")
+    r = _run("task1_float16_v1", "-m", "1024", "-n", "768", "-k", "512", "-w", "2", "-t", "5", "--seed", "0",
+             "--dist", "uniform", "--gpus", str(gpus), "--allgather", mode)
+    if mode == "nvls" and r.returncode != 0 and "multicast" in r.stderr + r.stdout:
+        pytest.skip("no NVLS multicast on these GPUs")
+    assert r.returncode == 0, r.stdout + r.stderr
+    res, sh = RESULT.search(r.stdout), SHARDED.search(r.stdout)
+    assert res and sh, r.stdout
+    assert float(res.group(1)) > 0 and float(res.group(2)) <= 2e-3
+    assert int(sh.group(1)) == gpus and sh.group(2) == mode and sh.group(3) == "1"
+
+
 def test_cli_help_and_errors(built):
     r = _run("task1_float16_v1", "-h")
     assert r.returncode == 0 and "-m arg" in r.stdout and "--n_warmup" in r.stdout
