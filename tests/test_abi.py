@@ -113,3 +113,25 @@ def test_peer_gemm_rejects_bad_arguments_without_gpu():
     assert vk.lib.vk_gemm_peers(ctypes.byref(a), nul, 2) == vk.VK_ERR_INVALID_ARGUMENT
     a.dtype = vk.DTYPE_F32
     assert vk.lib.vk_gemm_peers(ctypes.byref(a), peers, 1) == vk.VK_ERR_UNSUPPORTED
+
+
+def test_multicast_entry_points_reject_bad_arguments_without_gpu():
+    import ctypes
+
+    import vibekernel_b200 as vk
+    a = vk.GemmArgs()
+    a.m = a.n = a.k = 16
+    assert vk.lib.vk_gemm_mc(ctypes.byref(a), None) == vk.VK_ERR_INVALID_ARGUMENT
+    assert "C_mc is NULL" in vk.last_error()
+    assert vk.lib.vk_mc_supported(0, None) == vk.VK_ERR_INVALID_ARGUMENT
+    ptrs = (ctypes.c_void_p * 1)()
+    mc = ctypes.c_void_p()
+    assert vk.lib.vk_mc_alloc(0, None, 1 << 20, ptrs, ctypes.byref(mc)) == vk.VK_ERR_INVALID_ARGUMENT
+    assert vk.lib.vk_mc_free(ctypes.c_void_p(0x1234)) == vk.VK_ERR_INVALID_ARGUMENT
+    assert "not a multicast pointer" in vk.last_error()
+    assert vk.lib.vk_mc_detach(None) == vk.VK_ERR_INVALID_ARGUMENT
+    assert vk.lib.vk_mc_attach(None, None, None, None) == vk.VK_ERR_INVALID_ARGUMENT
+    team = ctypes.c_void_p()
+    share = (ctypes.c_int64 * 3)()
+    assert vk.lib.vk_mc_create(0, 0, 1 << 20, ctypes.byref(team), share) == vk.VK_ERR_INVALID_ARGUMENT
+    assert vk.lib.vk_mc_import(0, 2, None, ctypes.byref(team)) == vk.VK_ERR_INVALID_ARGUMENT
